@@ -1,0 +1,141 @@
+/*
+ * microserve-b200: C ABI of the B200 (sm_100a) FP8 decoder-layer kernels.
+ *
+ * Every entry point takes raw device pointers, explicit sizes and a
+ * cudaStream_t passed as `void*`, enqueues its kernels on that stream and
+ * returns without synchronising. None allocates device memory: callers own
+ * every buffer, including the scratch `workspace` some kernels need (query
+ * its size with the matching *_workspace_size function). All entry points are
+ * CUDA-graph capturable.
+ *
+ * Return codes: MS_OK (0) or a negative MS_ERR_* code; ms_last_error() then
+ * returns a message (thread-local). Tensor layouts are row-major and
+ * contiguous unless a stride argument says otherwise; fp16 is IEEE half,
+ * fp8 is e4m3 ("float8_e4m3fn"), scales are fp32.
+ *
+ * FP8 encoding (bit-exact with the reference):
+ *   scale = max(amax, 1e-8) / 448;  code = e4m3_rn_satfinite(clamp(x / scale, -448, 448))
+ *
+ * Each declaration names the reference interface it replaces
+ * (gssg1/microserve, path:line).
+ */
+#ifndef MICROSERVE_B200_H_
+#define MICROSERVE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MS_OK 0
+#define MS_ERR_INVALID (-1)     /* bad argument: null pointer, negative or unsupported size */
+#define MS_ERR_UNSUPPORTED (-2) /* shape outside what the kernels implement (e.g. head_dim != 128) */
+#define MS_ERR_CUDA (-3)        /* a CUDA runtime call failed; see ms_last_error() */
+#define MS_ERR_WORKSPACE (-4)   /* workspace smaller than the *_workspace_size result */
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int ms_version(void);
+
+/* Message for the last non-zero return code on this thread. */
+const char* ms_last_error(void);
+
+/* Reads and clears the device status word of the current device. Kernels
+ * that wait on barriers give up after a bounded time, record a non-zero code
+ * there (1 = tensor-core pipeline timeout, 2 = peer timeout) and return.
+ * Synchronises `stream`. */
+int ms_get_device_status(int* status, void* stream);
+
+/* Per-row dynamic FP8 quantisation of an fp16 matrix.
+ *   x [M, K] fp16 with row stride ldx (elements) -> xq [M, K] e4m3, sx [M] fp32.
+ * Replaces `_quantize_fp8_rows` (microserve/layers/fp8_linear.py:14-23). The
+ * same call quantises weights offline with one scale per output channel
+ * (microserve/layers/fp8_linear.py:49-56, FP8DynamicLinear.__init__). */
+int ms_quantize_rows_fp8(const void* x, int64_t ldx, int64_t M, int64_t K, void* xq, float* sx, void* stream);
+
+/* W8A8 FP8 GEMM with per-row x per-channel dequant:
+ *   y [M, N] fp16 = fp16((xq [M,K] . wq [N,K]^T) * sx[m] * sw[n]) (+ bias[n], fp16 add)
+ * Replaces `_fp8_mm` and FP8DynamicLinear.forward
+ * (microserve/layers/fp8_linear.py:26-45, :64-80). bias may be NULL.
+ * workspace: at least ms_fp8_gemm_workspace_size(M, N, K) bytes (may be 0). */
+size_t ms_fp8_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+int ms_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias, void* y,
+                int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+
+/* RMSNorm over rows of H (H % 16 == 0), optionally fused with the residual
+ * add and an FP8 quantisation of the output:
+ *   residual == NULL: y = fp16(fp16(x * rsqrt(mean(x^2) + eps)) * weight)
+ *   residual != NULL: r = fp16(x + residual) -> residual_out; y = norm(r)
+ *   y (may be NULL) fp16 [M, H]; yq/sy (may be NULL) = ms_quantize_rows_fp8(y)
+ * Replaces RMSNorm.forward with `_rmsnorm_kernel` / `_residual_rmsnorm_kernel`
+ * (microserve/layers/layernorm.py:7-42, :59-85). residual_out may alias residual. */
+int ms_rmsnorm(const void* x, const void* residual, const void* weight, int64_t M, int64_t H, float eps,
+               void* residual_out, void* y, void* yq, float* sy, void* stream);
+
+/* SiLU-and-mul over gu [M, 2I] (gate | up), I % 16 == 0:
+ *   a = fp16(fp16(silu(gate)) * up) -> out [M, I] (may be NULL); aq/sa (may be NULL) its FP8 rows.
+ * Replaces SiluAndMul (microserve/layers/activation.py:5-8) followed by
+ * `_quantize_fp8_rows` of down_proj's input (microserve/layers/fp8_linear.py:71-73). */
+int ms_silu_mul(const void* gu, int64_t M, int64_t I, void* out, void* aq, float* sa, void* stream);
+
+/* FP8 KV-cache store: per (token, kv head) scale + e4m3 codes scattered to slots.
+ *   k, v [T, kv_heads, head_dim] fp16; slots [T] int64 (negative = skip)
+ *   k_cache, v_cache [num_blocks, block_size, kv_heads, head_dim] e4m3
+ *   k_scale, v_scale [num_blocks, block_size, kv_heads] fp32
+ * Replaces store_fp8_kvcache (microserve/layers/fp8_kv_cache.py:11-61). head_dim must be 128. */
+int ms_store_kv_fp8(const void* k, const void* v, int64_t T, int kv_heads, int head_dim, const int64_t* slots,
+                    void* k_cache, void* v_cache, float* k_scale, float* v_scale, void* stream);
+
+/* Attention prologue of Qwen3Attention.forward fused in one pass over the QKV
+ * projection output qkv [T, (q_heads + 2 kv_heads) * head_dim] fp16:
+ * per-head q/k RMSNorm (skipped when q_norm_w == NULL), neox RoPE from fp16
+ * tables cos/sin [max_position, head_dim / 2] at positions [T] int64, then
+ *   q_out [T, q_heads, head_dim] fp16,
+ *   k_out / v_out [T, kv_heads, head_dim] fp16 (each may be NULL),
+ *   FP8 store of k and v into the cache at slots (skipped when slots == NULL).
+ * Replaces microserve/models/qwen3.py:44-53 (q/k norm: layers/layernorm.py:82-85,
+ * RoPE: layers/rotary_embedding.py:24-31) and the store of attention.py:41-43. */
+int ms_qkv_post(const void* qkv, int64_t T, int q_heads, int kv_heads, int head_dim, const void* q_norm_w,
+                const void* k_norm_w, float eps, const int64_t* positions, const void* cos_tab, const void* sin_tab,
+                const int64_t* slots, void* q_out, void* k_out, void* v_out, void* k_cache, void* v_cache,
+                float* k_scale, float* v_scale, void* stream);
+
+/* Paged FP8-KV decode attention, one query token per sequence.
+ *   q [B, Hq, head_dim] fp16; seqlens [B] int32; block_tables [B, max_blocks] int32
+ *   caches as in ms_store_kv_fp8; out [B, Hq, head_dim] fp16 (0 for seqlens == 0)
+ * Hq % Hkv == 0, Hq / Hkv <= 8, head_dim == 128, block_size % 16 == 0.
+ * Replaces fp8_decode_attention (microserve/layers/fp8_decode_attention.py:8-101).
+ * workspace: ms_paged_decode_workspace_size(...) bytes (0 when no context split is used). */
+size_t ms_paged_decode_workspace_size(int B, int Hq, int Hkv, int max_blocks, int block_size);
+int ms_paged_decode_fp8(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
+                        const float* v_scale, const int32_t* seqlens, const int32_t* block_tables, void* out, int B,
+                        int Hq, int Hkv, int head_dim, int block_size, int max_blocks, float softmax_scale,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Causal chunked-prefill attention over the paged FP8 cache, any number of
+ * sequences: sequence s has queries q[cu_q[s] .. cu_q[s+1]) at positions
+ * kv_lens[s] - q_len_s .. kv_lens[s] - 1 and attends to its first kv_lens[s]
+ * cached tokens (which must already hold this chunk's keys/values).
+ *   q, out [total_q, Hq, head_dim] fp16; cu_q [num_seqs + 1] int32; kv_lens [num_seqs] int32
+ *   block_tables [num_seqs, max_blocks] int32; block_size % 64 == 0
+ * Replaces fp8_chunk_prefill_attention
+ * (microserve/layers/fp8_chunk_prefill_attention.py:8-109; one sequence per call there). */
+int ms_paged_prefill_fp8(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
+                         const float* v_scale, const int32_t* block_tables, const int32_t* cu_q,
+                         const int32_t* kv_lens, void* out, int num_seqs, int64_t total_q, int Hq, int Hkv,
+                         int head_dim, int block_size, int max_blocks, float softmax_scale, void* stream);
+
+/* Causal varlen prefill attention over fresh fp16 q, k, v (first chunk of
+ * each sequence): q, out [total, Hq, head_dim]; k, v [total, Hkv, head_dim];
+ * cu [num_seqs + 1] int32 (same offsets for queries and keys).
+ * Replaces the FP8-KV PREFILL branch's flash_attn_varlen_func call
+ * (microserve/layers/attention.py:49-55). */
+int ms_varlen_prefill(const void* q, const void* k, const void* v, const int32_t* cu, void* out, int num_seqs,
+                      int64_t total, int Hq, int Hkv, int head_dim, float softmax_scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MICROSERVE_B200_H_ */

@@ -1,0 +1,158 @@
+// Shared device helpers for the microserve-b200 kernels (sm_100a only).
+//
+// Numerics contract: every FP8 encode in this library is
+//   scale = max(amax, 1e-8f) / 448.0f       (IEEE fp32 divide)
+//   q     = e4m3(clamp(x / scale, -448, 448)) (IEEE divide, round-to-nearest-even, satfinite)
+// which is the formula of the reference's Triton kernels
+// (microserve/layers/fp8_linear.py:20-21, microserve/layers/fp8_kv_cache.py:34-37).
+// The library is compiled without --use_fast_math so that `/` is div.rn.f32.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define MS_FP8_MAX 448.0f
+
+namespace ms {
+
+// ---------------------------------------------------------------------------
+// Device status word: kernels that wait on barriers never spin forever; on a
+// timeout they record a code here and return. The host reads it with
+// ms_get_device_status().
+// ---------------------------------------------------------------------------
+enum DeviceStatus : int {
+  kStatusOk = 0,
+  kStatusMbarTimeout = 1,
+  kStatusPeerTimeout = 2,
+};
+
+extern __device__ int g_device_status;
+
+__device__ __forceinline__ void set_device_status(int code) {
+  atomicCAS(&g_device_status, 0, code);
+}
+
+// ---------------------------------------------------------------------------
+// FP8 helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float fp8_scale_from_amax(float amax) {
+  return fmaxf(amax, 1e-8f) / MS_FP8_MAX;
+}
+
+// Encode two fp32 values (already divided by the scale) into two e4m3 bytes,
+// clamped to +-448 first (the clamp is a no-op for finite values under
+// satfinite, kept for NaN-free parity with the reference's explicit clamp).
+__device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float a, float b) {
+  a = fminf(fmaxf(a, -MS_FP8_MAX), MS_FP8_MAX);
+  b = fminf(fmaxf(b, -MS_FP8_MAX), MS_FP8_MAX);
+  __nv_fp8x2_storage_t r = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  return (uint16_t)r;
+}
+
+__device__ __forceinline__ uint8_t f32_to_e4m3(float a) {
+  a = fminf(fmaxf(a, -MS_FP8_MAX), MS_FP8_MAX);
+  return (uint8_t)__nv_cvt_float_to_fp8(a, __NV_SATFINITE, __NV_E4M3);
+}
+
+// Two e4m3 bytes (low byte = first element) -> half2, exact.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(v));
+  return r;
+}
+
+__device__ __forceinline__ float e4m3_to_f32(uint8_t v) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)v, __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// Warp / block reductions
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide reduction; `smem` must hold >= 32 floats. All threads get the result.
+template <bool kMax>
+__device__ __forceinline__ float block_reduce(float v, float* smem) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = kMax ? warp_max(v) : warp_sum(v);
+  __syncthreads();
+  if (lane == 0) smem[wid] = v;
+  __syncthreads();
+  float r = (lane < nw) ? smem[lane] : (kMax ? 0.f : 0.f);
+  if (wid == 0) {
+    r = kMax ? warp_max(r) : warp_sum(r);
+    if (lane == 0) smem[0] = r;
+  }
+  __syncthreads();
+  return smem[0];
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier helpers (bounded waits)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait until the barrier's phase `phase` completed. Gives up after ~`limit`
+// polls (each try_wait already suspends for a hardware-defined interval),
+// records kStatusMbarTimeout and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t limit = (1u << 24)) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if (i > 64) __nanosleep(32);
+  }
+  set_device_status(kStatusMbarTimeout);
+  return false;
+}
+
+}  // namespace ms

@@ -1,0 +1,351 @@
+// Paged FP8-KV decode attention (one query token per sequence), the
+// reference's `_fp8_decode_flashAttention` (microserve/layers/fp8_decode_attention.py:8-59):
+//   o[b, hq] = softmax_t(q[b,hq] . (k_fp8[t] * k_scale[t]) * sm_scale) . (v_fp8[t] * v_scale[t])
+// over t < cache_seqlens[b], pages looked up in block_tables[b]. Rows with
+// cache_seqlens == 0 produce 0.
+//
+// B200 design:
+//  * One CTA per (split, kv head, sequence); the G = Hq/Hkv query heads that
+//    share a kv head are processed together so every K/V byte is read once
+//    (the reference re-reads K/V once per query head).
+//  * K and V go straight from HBM to registers with 16-byte loads (no shared
+//    memory), are widened e4m3 -> f16 in registers (exact), and both products
+//    run on the tensor cores with mma.m16n8k16 (f16 in, f32 accumulate):
+//        S^T[tok, head] = K[tok, d] . Q^T[d, head]      (M = 16 tokens, N = 8 heads)
+//        O^T[d, head]  += V^T[d, tok] . P'^T[tok, head] (M = 16 of d, N = 8 heads)
+//    The head_dim axis of each product is permuted so that every thread's
+//    fragment comes from contiguous bytes it loaded itself; Q and O use the
+//    same permutation, so results are unchanged. The per-token k scale is
+//    applied to the fp32 scores; the per-token v scale is folded into P'
+//    (P' = p * v_scale) before it is rounded to f16 for the second product.
+//    P' changes from the accumulator layout to the operand layout with
+//    movmatrix (an in-register 8x8 transpose).
+//  * Online softmax in the exp2 domain; warps of a CTA interleave 16-token
+//    tiles and are merged through shared memory at the end. Long contexts with
+//    few sequences are split over CTAs (flash-decoding); partial (m, l, o)
+//    rows go to a workspace and a second kernel merges them.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ms {
+namespace {
+
+constexpr int kD = 128;
+constexpr int kWarps = 4;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+struct DecodeArgs {
+  const __half* q;            // [B, Hq, D]
+  const uint8_t* k_cache;     // [NB, BS, Hkv, D]
+  const uint8_t* v_cache;
+  const float* k_scale;       // [NB, BS, Hkv]
+  const float* v_scale;
+  const int32_t* seqlens;     // [B]
+  const int32_t* block_tables;  // [B, max_blocks]
+  __half* out;                // [B, Hq, D]
+  float* ws_o;                // [B, Hq, S, D]   (S > 1 only)
+  float* ws_ml;               // [B, Hq, S, 2]
+  int B, Hq, Hkv, block_size, max_blocks, splits;
+  float scale_log2;           // softmax_scale * log2(e)
+};
+
+__global__ void __launch_bounds__(kWarps * 32) decode_kernel(DecodeArgs a) {
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int G = a.Hq / a.Hkv;
+  const int L = a.seqlens[b];
+  const int ntiles = (L + 15) >> 4;
+  const int tps = (ntiles + a.splits - 1) / a.splits;
+  const int t_begin = split * tps;
+  const int t_end = min(ntiles, t_begin + tps);
+
+  // Q fragment: head g of this group, d = 64j + 16c + [0,16).
+  uint32_t qf[2][8];
+  {
+    const bool valid = g < G;
+    const __half* qrow = a.q + ((int64_t)b * a.Hq + kvh * G + (valid ? g : 0)) * kD;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint4 u0 = valid ? *reinterpret_cast<const uint4*>(qrow + 64 * j + 16 * c) : make_uint4(0, 0, 0, 0);
+      uint4 u1 = valid ? *reinterpret_cast<const uint4*>(qrow + 64 * j + 16 * c + 8) : make_uint4(0, 0, 0, 0);
+      qf[j][0] = u0.x; qf[j][1] = u0.y; qf[j][2] = u0.z; qf[j][3] = u0.w;
+      qf[j][4] = u1.x; qf[j][5] = u1.y; qf[j][6] = u1.z; qf[j][7] = u1.w;
+    }
+  }
+
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};  // heads 2c, 2c+1
+  float l_run[2] = {0.f, 0.f};              // per-thread partial sums (reduced over g at the end)
+
+  const int64_t tok_stride = (int64_t)a.Hkv * kD;  // bytes between consecutive tokens of a page
+  const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
+
+  for (int tile = t_begin + warp; tile < t_end; tile += kWarps) {
+    const int p0 = tile << 4;
+    const int page = p0 / a.block_size;
+    const int off = p0 - page * a.block_size;
+    const int64_t phys = bt[page];
+    const int64_t tok0 = phys * a.block_size + off;  // global token slot of row 0 of this tile
+    const uint8_t* kbase = a.k_cache + (tok0 * a.Hkv + kvh) * kD;
+    const uint8_t* vbase = a.v_cache + (tok0 * a.Hkv + kvh) * kD;
+    // K rows g, g+8: bytes [16c, 16c+16) and [64+16c, ...)
+    uint4 k0a = ldg_nc_v4(kbase + g * tok_stride + 16 * c);
+    uint4 k0b = ldg_nc_v4(kbase + g * tok_stride + 64 + 16 * c);
+    uint4 k1a = ldg_nc_v4(kbase + (g + 8) * tok_stride + 16 * c);
+    uint4 k1b = ldg_nc_v4(kbase + (g + 8) * tok_stride + 64 + 16 * c);
+    // V rows 2c, 2c+1, 2c+8, 2c+9: bytes [16g, 16g+16)
+    uint4 v0 = ldg_nc_v4(vbase + (2 * c) * tok_stride + 16 * g);
+    uint4 v1 = ldg_nc_v4(vbase + (2 * c + 1) * tok_stride + 16 * g);
+    uint4 v2 = ldg_nc_v4(vbase + (2 * c + 8) * tok_stride + 16 * g);
+    uint4 v3 = ldg_nc_v4(vbase + (2 * c + 9) * tok_stride + 16 * g);
+    const float ks0 = a.k_scale[(tok0 + g) * a.Hkv + kvh];
+    const float ks1 = a.k_scale[(tok0 + g + 8) * a.Hkv + kvh];
+    const float vs0 = a.v_scale[(tok0 + g) * a.Hkv + kvh];
+    const float vs1 = a.v_scale[(tok0 + g + 8) * a.Hkv + kvh];
+    const bool tail = p0 + 16 > L;
+    if (tail) {  // zero V rows past the end so stale bytes can never reach the product
+      if (p0 + 2 * c >= L) v0 = make_uint4(0, 0, 0, 0);
+      if (p0 + 2 * c + 1 >= L) v1 = make_uint4(0, 0, 0, 0);
+      if (p0 + 2 * c + 8 >= L) v2 = make_uint4(0, 0, 0, 0);
+      if (p0 + 2 * c + 9 >= L) v3 = make_uint4(0, 0, 0, 0);
+    }
+
+    // ---- S^T = K . Q^T -------------------------------------------------
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const uint32_t kw0[8] = {k0a.x, k0a.y, k0a.z, k0a.w, k0b.x, k0b.y, k0b.z, k0b.w};
+      const uint32_t kw1[8] = {k1a.x, k1a.y, k1a.z, k1a.w, k1b.x, k1b.y, k1b.z, k1b.w};
+#pragma unroll
+      for (int st = 0; st < 8; ++st) {
+        const int j = st >> 2, w = st & 3;
+        const uint32_t r0 = e4m3x2_to_f16x2((uint16_t)(kw0[st] & 0xffff));
+        const uint32_t r2 = e4m3x2_to_f16x2((uint16_t)(kw0[st] >> 16));
+        const uint32_t r1 = e4m3x2_to_f16x2((uint16_t)(kw1[st] & 0xffff));
+        const uint32_t r3 = e4m3x2_to_f16x2((uint16_t)(kw1[st] >> 16));
+        mma16816(s, r0, r1, r2, r3, qf[j][2 * w], qf[j][2 * w + 1]);
+      }
+    }
+    // s[0], s[1]: token g, heads 2c, 2c+1; s[2], s[3]: token g+8.
+    const bool ok0 = p0 + g < L, ok1 = p0 + g + 8 < L;
+    s[0] = ok0 ? s[0] * ks0 * a.scale_log2 : -INFINITY;
+    s[1] = ok0 ? s[1] * ks0 * a.scale_log2 : -INFINITY;
+    s[2] = ok1 ? s[2] * ks1 * a.scale_log2 : -INFINITY;
+    s[3] = ok1 ? s[3] * ks1 * a.scale_log2 : -INFINITY;
+
+    float tmax0 = fmaxf(s[0], s[2]), tmax1 = fmaxf(s[1], s[3]);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      tmax0 = fmaxf(tmax0, __shfl_xor_sync(0xffffffffu, tmax0, o));
+      tmax1 = fmaxf(tmax1, __shfl_xor_sync(0xffffffffu, tmax1, o));
+    }
+    const float mn0 = fmaxf(m_run[0], tmax0), mn1 = fmaxf(m_run[1], tmax1);
+    // The first tile always holds token p0 < L, so mn is finite here.
+    const float al0 = ex2(m_run[0] - mn0), al1 = ex2(m_run[1] - mn1);
+    m_run[0] = mn0;
+    m_run[1] = mn1;
+    const float p00 = ex2(s[0] - mn0), p01 = ex2(s[1] - mn1);
+    const float p10 = ex2(s[2] - mn0), p11 = ex2(s[3] - mn1);
+    l_run[0] = l_run[0] * al0 + p00 + p10;
+    l_run[1] = l_run[1] * al1 + p01 + p11;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      acc[i][0] *= al0; acc[i][1] *= al1;
+      acc[i][2] *= al0; acc[i][3] *= al1;
+    }
+    // P'^T operand: fold the per-token v scale, round to f16, transpose.
+    const uint32_t x0 = pack_h2(p00 * vs0, p01 * vs0);
+    const uint32_t x1 = pack_h2(p10 * vs1, p11 * vs1);
+    const uint32_t pb0 = movmatrix_trans(x0);
+    const uint32_t pb1 = movmatrix_trans(x1);
+
+    // ---- O^T += V^T . P'^T ---------------------------------------------
+    const uint32_t va[4] = {v0.x, v0.y, v0.z, v0.w};
+    const uint32_t vb[4] = {v1.x, v1.y, v1.z, v1.w};
+    const uint32_t vc[4] = {v2.x, v2.y, v2.z, v2.w};
+    const uint32_t vd[4] = {v3.x, v3.y, v3.z, v3.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int w = i >> 1;
+      // bytes 2i, 2i+1 of the 16-byte chunks -> (row 2c, row 2c+1) pairs
+      const uint32_t sel = (i & 1) ? 0x7362u : 0x5140u;
+      const uint32_t lo = prmt(va[w], vb[w], sel);  // {R0[2i], R1[2i], R0[2i+1], R1[2i+1]}
+      const uint32_t hi = prmt(vc[w], vd[w], sel);
+      const uint32_t a0 = e4m3x2_to_f16x2((uint16_t)(lo & 0xffff));
+      const uint32_t a1 = e4m3x2_to_f16x2((uint16_t)(lo >> 16));
+      const uint32_t a2 = e4m3x2_to_f16x2((uint16_t)(hi & 0xffff));
+      const uint32_t a3 = e4m3x2_to_f16x2((uint16_t)(hi >> 16));
+      mma16816(acc[i], a0, a1, a2, a3, pb0, pb1);
+    }
+  }
+
+  // ---- merge warps ---------------------------------------------------------
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], o);
+    l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], o);
+  }
+  __shared__ float sm_m[kWarps][8], sm_l[kWarps][8];
+  __shared__ float sm_o[kWarps][8][kD + 4];
+  if (g == 0) {
+    sm_m[warp][2 * c] = m_run[0];
+    sm_m[warp][2 * c + 1] = m_run[1];
+    sm_l[warp][2 * c] = l_run[0];
+    sm_l[warp][2 * c + 1] = l_run[1];
+  }
+  // acc[i][0..1]: d = 16g + 2i, heads 2c, 2c+1; acc[i][2..3]: d = 16g + 2i + 1.
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    sm_o[warp][2 * c][16 * g + 2 * i] = acc[i][0];
+    sm_o[warp][2 * c + 1][16 * g + 2 * i] = acc[i][1];
+    sm_o[warp][2 * c][16 * g + 2 * i + 1] = acc[i][2];
+    sm_o[warp][2 * c + 1][16 * g + 2 * i + 1] = acc[i][3];
+  }
+  __syncthreads();
+  // Thread t handles (head = t / 16, d = 8 * (t % 16) .. +8) for heads < G.
+  for (int item = threadIdx.x; item < G * 16; item += blockDim.x) {
+    const int h = item >> 4, d0 = (item & 15) * 8;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w][h]);
+    float Lsum = 0.f, o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float wt = (sm_m[w][h] == -INFINITY) ? 0.f : ex2(sm_m[w][h] - M);
+      Lsum += sm_l[w][h] * wt;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] += sm_o[w][h][d0 + e] * wt;
+    }
+    const int hq = kvh * G + h;
+    if (a.splits == 1) {
+      const float inv = (L > 0 && Lsum > 0.f) ? 1.f / Lsum : 0.f;
+      uint4 packed;
+      packed.x = pack_h2(o[0] * inv, o[1] * inv);
+      packed.y = pack_h2(o[2] * inv, o[3] * inv);
+      packed.z = pack_h2(o[4] * inv, o[5] * inv);
+      packed.w = pack_h2(o[6] * inv, o[7] * inv);
+      *reinterpret_cast<uint4*>(a.out + ((int64_t)b * a.Hq + hq) * kD + d0) = packed;
+    } else {
+      const int64_t row = ((int64_t)b * a.Hq + hq) * a.splits + split;
+      float* dst = a.ws_o + row * kD + d0;
+      *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<float4*>(dst + 4) = make_float4(o[4], o[5], o[6], o[7]);
+      if (d0 == 0) {
+        a.ws_ml[row * 2] = M;
+        a.ws_ml[row * 2 + 1] = Lsum;
+      }
+    }
+  }
+}
+
+// Merge split partials: one CTA per (sequence, q head), one thread per d.
+__global__ void __launch_bounds__(kD) decode_merge_kernel(const float* __restrict__ ws_o,
+                                                          const float* __restrict__ ws_ml,
+                                                          const int32_t* __restrict__ seqlens, int Hq, int splits,
+                                                          __half* __restrict__ out) {
+  const int b = blockIdx.y, hq = blockIdx.x, d = threadIdx.x;
+  const int64_t row0 = ((int64_t)b * Hq + hq) * splits;
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, ws_ml[(row0 + s) * 2]);
+  float Lsum = 0.f, o = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float m = ws_ml[(row0 + s) * 2];
+    const float wt = (m == -INFINITY) ? 0.f : ex2(m - M);
+    Lsum += ws_ml[(row0 + s) * 2 + 1] * wt;
+    o += ws_o[(row0 + s) * kD + d] * wt;
+  }
+  const float r = (seqlens[b] > 0 && Lsum > 0.f) ? o / Lsum : 0.f;
+  out[((int64_t)b * Hq + hq) * kD + d] = __float2half_rn(r);
+}
+
+}  // namespace
+
+int decode_num_splits(int B, int Hkv, int max_blocks, int block_size, int num_sms) {
+  const int ctas = B * Hkv;
+  const int target = num_sms * 4;
+  if (ctas >= target) return 1;
+  const int max_ctx = max_blocks * block_size;
+  // at least 8 tiles (128 tokens) per split so each warp has work
+  const int max_split = max(1, (max_ctx + 127) / 128);
+  int s = (target + ctas - 1) / ctas;
+  return min(s, min(max_split, 256));
+}
+
+size_t decode_workspace_bytes(int B, int Hq, int splits) {
+  if (splits <= 1) return 0;
+  return (size_t)B * Hq * splits * (kD + 2) * sizeof(float);
+}
+
+cudaError_t launch_decode_attention(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
+                                    const float* v_scale, const int32_t* seqlens, const int32_t* block_tables,
+                                    void* out, int B, int Hq, int Hkv, int head_dim, int block_size, int max_blocks,
+                                    float softmax_scale, int splits, void* workspace, cudaStream_t stream) {
+  if (head_dim != kD || Hq % Hkv != 0 || Hq / Hkv > 8 || block_size % 16 != 0 || splits < 1)
+    return cudaErrorInvalidValue;
+  if (B == 0) return cudaSuccess;
+  DecodeArgs a;
+  a.q = (const __half*)q;
+  a.k_cache = (const uint8_t*)k_cache;
+  a.v_cache = (const uint8_t*)v_cache;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.seqlens = seqlens;
+  a.block_tables = block_tables;
+  a.out = (__half*)out;
+  a.ws_o = (float*)workspace;
+  a.ws_ml = splits > 1 ? (float*)workspace + (size_t)B * Hq * splits * kD : nullptr;
+  a.B = B;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.block_size = block_size;
+  a.max_blocks = max_blocks;
+  a.splits = splits;
+  a.scale_log2 = softmax_scale * kLog2e;
+  dim3 grid(splits, Hkv, B);
+  decode_kernel<<<grid, kWarps * 32, 0, stream>>>(a);
+  if (splits > 1) {
+    dim3 g2(Hq, B);
+    decode_merge_kernel<<<g2, kD, 0, stream>>>(a.ws_o, a.ws_ml, seqlens, Hq, splits, (__half*)out);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace ms

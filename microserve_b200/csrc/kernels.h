@@ -1,0 +1,43 @@
+// Internal launcher declarations (C++), wrapped by the C ABI in capi.cu.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ms {
+
+cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t M, int K, void* xq, float* sx,
+                                 cudaStream_t stream);
+cudaError_t launch_rmsnorm(const void* x, const void* residual, const void* weight, int64_t M, int H, float eps,
+                           void* residual_out, void* y, void* yq, float* sy, cudaStream_t stream);
+cudaError_t launch_silu_mul(const void* gu, int64_t M, int I, void* out, void* aq, float* sa, cudaStream_t stream);
+
+cudaError_t launch_store_kv_fp8(const void* k, const void* v, int64_t T, int kv_heads, int head_dim,
+                                const int64_t* slots, void* k_cache, void* v_cache, float* k_scale, float* v_scale,
+                                cudaStream_t stream);
+cudaError_t launch_qkv_post(const void* qkv, int64_t T, int q_heads, int kv_heads, int head_dim, const void* q_norm_w,
+                            const void* k_norm_w, float eps, const int64_t* positions, const void* cos_tab,
+                            const void* sin_tab, const int64_t* slots, void* q_out, void* k_out, void* v_out,
+                            void* k_cache, void* v_cache, float* k_scale, float* v_scale, cudaStream_t stream);
+
+int decode_num_splits(int B, int Hkv, int max_blocks, int block_size, int num_sms);
+size_t decode_workspace_bytes(int B, int Hq, int splits);
+cudaError_t launch_decode_attention(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
+                                    const float* v_scale, const int32_t* seqlens, const int32_t* block_tables,
+                                    void* out, int B, int Hq, int Hkv, int head_dim, int block_size, int max_blocks,
+                                    float softmax_scale, int splits, void* workspace, cudaStream_t stream);
+
+cudaError_t launch_prefill_attention(bool paged, const void* q, const void* k16, const void* v16,
+                                     const void* k_cache, const void* v_cache, const float* k_scale,
+                                     const float* v_scale, const int32_t* block_tables, const int32_t* cu_q,
+                                     const int32_t* kv_lens, void* out, int num_seqs, int total_q, int Hq, int Hkv,
+                                     int head_dim, int block_size, int max_blocks, float softmax_scale,
+                                     cudaStream_t stream);
+
+void gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* splits_out);
+size_t gemm_workspace_bytes(int M, int N, int K, int num_sms);
+cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,
+                            void* y, int M, int N, int K, void* workspace, size_t workspace_bytes, int num_sms,
+                            cudaStream_t stream);
+
+}  // namespace ms

@@ -1,0 +1,6 @@
+// The device status word shared by every kernel of the library (see common.cuh).
+#include "common.cuh"
+
+namespace ms {
+__device__ int g_device_status = 0;
+}  // namespace ms

@@ -1,0 +1,54 @@
+"""Tensor-parallel process group state.
+
+One process per GPU. `init_tensor_parallel()` records the group every
+TP-aware layer uses; with no group (the default) tp_size == 1 and every layer
+behaves exactly like the reference's single-GPU layers.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+_GROUP = None
+_RANK = 0
+_SIZE = 1
+
+
+def init_tensor_parallel(group=None) -> None:
+    """Use `group` (default: the world) for tensor parallelism."""
+    global _GROUP, _RANK, _SIZE
+    if not dist.is_initialized():
+        raise RuntimeError("torch.distributed must be initialised before init_tensor_parallel()")
+    _GROUP = group if group is not None else dist.group.WORLD
+    _RANK = dist.get_rank(_GROUP)
+    _SIZE = dist.get_world_size(_GROUP)
+
+
+def reset_tensor_parallel() -> None:
+    global _GROUP, _RANK, _SIZE
+    _GROUP, _RANK, _SIZE = None, 0, 1
+
+
+def tp_rank() -> int:
+    return _RANK
+
+
+def tp_size() -> int:
+    return _SIZE
+
+
+def tp_group():
+    return _GROUP
+
+
+def all_reduce_(x: torch.Tensor) -> torch.Tensor:
+    """In-place sum over the TP group (identity when tp_size == 1)."""
+    if _SIZE > 1:
+        dist.all_reduce(x, group=_GROUP)
+    return x
+
+
+def all_reduce_max_(x: torch.Tensor) -> torch.Tensor:
+    if _SIZE > 1:
+        dist.all_reduce(x, op=dist.ReduceOp.MAX, group=_GROUP)
+    return x
