@@ -1,0 +1,508 @@
+#!/usr/bin/env python
+"""Benchmark: Qwen3-8B-shaped FP8 decode throughput.
+
+Workload (synthetic, seeded; no checkpoints or datasets exist offline):
+  Qwen3-8B shapes (36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128,
+  MLP 12288, vocab 151936), random N(0, 0.02) weights quantised to FP8 e4m3
+  per output channel, FP8 e4m3 KV cache in 256-token pages, fp16
+  activations; 256 sequences with prompt lengths uniform in [128, 1024]
+  (random.Random(0)), greedy decoding, tensor parallel over --gpus.
+
+value (`metric`, device-resident): decode steps of the whole batch (CUDA
+  graph replay of embedding -> 36 FP8 decoder layers -> norm -> LM head ->
+  greedy argmax) with every step's metadata already in HBM; the argmax of a
+  step is the next step's input. tok/s = batch * K / time of K steps.
+e2e: the full config-3 job through LLMEngine (add 256 requests of 512 output
+  tokens, step() until idle): prompts/metadata go host->device from pinned
+  memory and sampled tokens come back every step. tok/s = output tokens /
+  elapsed, plus ITL p50 (consecutive token-timestamp deltas).
+roofline: the dominant kernel of the decode step, timed alone on the step's
+  own inputs with CUDA events; algorithmic bytes per launch over that time.
+cpu_baseline: the CPU oracle (a restatement of the reference's FP8 path) on
+  the host cores for one decoder layer of the same decode step, scaled to
+  the full model.
+
+--impl reference times that CPU restatement alone (the reference has no
+B200 path of its own to run here: its kernels are Triton JIT kernels, see
+DESIGN.md).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+MODELS = {
+    "8b": dict(layers=36, hidden=4096, heads=32, kv_heads=8, inter=12288, vocab=151936, tie=False),
+    "0.6b": dict(layers=28, hidden=1024, heads=16, kv_heads=8, inter=3072, vocab=151936, tie=True),
+    "32b": dict(layers=64, hidden=5120, heads=64, kv_heads=8, inter=25600, vocab=151936, tie=False),
+}
+HEAD_DIM = 128
+BLOCK = 256
+
+
+def qwen3_cfg(name: str, max_pos: int = 40960):
+    from transformers import Qwen3Config
+    m = MODELS[name]
+    return Qwen3Config(vocab_size=m["vocab"], hidden_size=m["hidden"], intermediate_size=m["inter"],
+                       num_hidden_layers=m["layers"], num_attention_heads=m["heads"],
+                       num_key_value_heads=m["kv_heads"], head_dim=HEAD_DIM, max_position_embeddings=max_pos,
+                       rms_norm_eps=1e-6, tie_word_embeddings=m["tie"], hidden_act="silu", attention_bias=False)
+
+
+def prompts(n: int, lo: int, hi: int, vocab: int, seed: int = 0) -> list[list[int]]:
+    rng = random.Random(seed)
+    lens = [rng.randint(lo, hi) for _ in range(n)]
+    return [[rng.randrange(100, vocab) for _ in range(L)] for L in lens]
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (median SM clock, throttle reasons)."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- ours
+def build_engine(args, cfg, max_model_len):
+    from microserve_b200.Config import Config
+    from microserve_b200.engine.llm import LLMEngine
+    return LLMEngine(Config(hf_config=cfg, load_format="dummy", quantization="fp8_dynamic",
+                            kv_cache_dtype="fp8_e4m3", max_num_seqs=args.batch,
+                            max_num_batched_tokens=args.max_batched_tokens, max_model_len=max_model_len,
+                            tensor_parallel_size=args.gpus, gpu_memory_utilization=0.9, seed=0))
+
+
+def sync_all():
+    torch.cuda.synchronize()
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x: float) -> float:
+    if torch.distributed.is_initialized():
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+    return x
+
+
+def run_e2e(engine, reqs, out_len):
+    """Whole job through LLMEngine; returns (tok/s, itl_p50_ms, elapsed_s, h2d/step, d2h/step, steps)."""
+    from microserve_b200.engine.sequence import SamplingParams
+    runner = engine.runner
+    seqs = [engine.add(r, SamplingParams(temperature=0.0), max_tokens=out_len) for r in reqs]
+    h2d0 = runner.host_batch.bytes_uploaded
+    sync_all()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    start.record()
+    steps = 0
+    while not engine.is_idle():
+        engine.step()
+        steps += 1
+    end.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    elapsed = max_over_ranks(max(start.elapsed_time(end) / 1e3, wall))
+    out = sum(s.num_completion_tokens for s in seqs)
+    itl = [(b - a) * 1e3 for s in seqs for a, b in zip(s.token_timestamps, s.token_timestamps[1:])]
+    h2d = (runner.host_batch.bytes_uploaded - h2d0) / max(steps, 1)
+    d2h = out * 8 / max(steps, 1)
+    return out / elapsed, (statistics.median(itl) if itl else None), elapsed, h2d, d2h, steps
+
+
+def prepare_decode_batch(engine, reqs, steps_total):
+    """Prefill `reqs` through the engine, then lay out `steps_total` decode steps
+    of metadata for the whole batch in HBM (positions, slots, seqlens, tables)."""
+    from microserve_b200.engine.sequence import SamplingParams
+    runner = engine.runner
+    seqs = [engine.add(r, SamplingParams(temperature=0.0), max_tokens=10 ** 6) for r in reqs]
+    while any(s.gap > 1 or s.num_computed_tokens == 0 for s in seqs):
+        engine.step()
+    bm = engine.scheduler.block_manager
+    B = len(seqs)
+    pos = np.zeros((steps_total, B), np.int64)
+    slots = np.zeros((steps_total, B), np.int64)
+    for i, s in enumerate(seqs):
+        p0 = s.num_computed_tokens
+        need = (p0 + steps_total - 1) // BLOCK + 1
+        while len(s.block_table) < need:
+            s.block_table.append(bm._take_free())
+        for st in range(steps_total):
+            p = p0 + st
+            pos[st, i] = p
+            slots[st, i] = s.block_table[p // BLOCK] * BLOCK + p % BLOCK
+    gv = runner.graph_vars
+    width = gv["block_tables"].shape[1]
+    bt = np.full((B, width), -1, np.int32)
+    for i, s in enumerate(seqs):
+        bt[i, :len(s.block_table)] = s.block_table
+    ids0 = np.array([s.token_ids[s.num_computed_tokens] for s in seqs], np.int64)
+    dev = runner.device
+    return dict(seqs=seqs, pos=torch.from_numpy(pos).to(dev), slots=torch.from_numpy(slots).to(dev),
+                lens=torch.from_numpy((pos + 1).astype(np.int32)).to(dev), bt=torch.from_numpy(bt).to(dev),
+                ids0=torch.from_numpy(ids0).to(dev), ctx0=pos[0] + 1)
+
+
+@torch.inference_mode()
+def decode_step_runner(engine, batch):
+    runner = engine.runner
+    gv = runner.graph_vars
+    B = batch["ids0"].shape[0]
+    graph = runner.graphs[B]
+    gv["block_tables"][:B].copy_(batch["bt"])
+    gv["input_ids"][:B].copy_(batch["ids0"])
+
+    @torch.inference_mode()
+    def step(i):
+        gv["positions"][:B].copy_(batch["pos"][i])
+        gv["slot_mapping"][:B].copy_(batch["slots"][i])
+        gv["cache_seqlens"][:B].copy_(batch["lens"][i])
+        graph.replay()
+        gv["input_ids"][:B].copy_(gv["argmax"][:B])
+    return step
+
+
+def time_kernel(fn, iters=20, warm=3):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / 1e3 / iters
+
+
+@torch.inference_mode()
+def kernel_rooflines(engine, batch, step_idx, hbm_peak):
+    """Per-kernel achieved HBM bandwidth on the decode step's own inputs (layer 0)."""
+    from microserve_b200 import kernels
+    runner = engine.runner
+    model = runner.model
+    layer = model.model.layers[0]
+    attn = layer.self_attn.attn
+    B = batch["ids0"].shape[0]
+    Hq, Hkv = layer.self_attn.num_heads, layer.self_attn.num_kv_heads
+    dev = runner.device
+    q = torch.randn(B, Hq, HEAD_DIM, device=dev, dtype=torch.float16) * 0.2
+    lens = batch["lens"][step_idx]
+    out = torch.empty_like(q)
+    t_attn = time_kernel(lambda: kernels.paged_decode_fp8(q, attn.k_cache, attn.v_cache, attn.k_scale_cache,
+                                                          attn.v_scale_cache, lens, batch["bt"], HEAD_DIM ** -0.5,
+                                                          out=out))
+    ctx = lens.double().sum().item()
+    attn_bytes = ctx * Hkv * (2 * HEAD_DIM + 2 * 4) + 2 * B * Hq * HEAD_DIM * 2 + B * (4 + 4 * batch["bt"].shape[1])
+    res = {"decode_attention": dict(seconds=t_attn, bytes=attn_bytes, per_layer=1)}
+    lins = {"qkv_proj": layer.self_attn.qkv_proj, "o_proj": layer.self_attn.o_proj,
+            "gate_up_proj": layer.mlp.gate_up_proj, "down_proj": layer.mlp.down_proj}
+    for name, lin in lins.items():
+        x = torch.randn(B, lin.in_features, device=dev, dtype=torch.float16)
+        xq, sx = kernels.quantize_rows_fp8(x)
+        y = torch.empty(B, lin.out_features, device=dev, dtype=torch.float16)
+        t = time_kernel(lambda: kernels.fp8_gemm(xq, sx, lin.weight_fp8, lin.weight_scale, out=y))
+        byts = lin.out_features * lin.in_features + B * lin.in_features + 2 * B * lin.out_features \
+            + 4 * (B + lin.out_features)
+        res[name] = dict(seconds=t, bytes=byts, per_layer=1)
+    for v in res.values():
+        v["achieved_gbs"] = v["bytes"] / v["seconds"] / 1e9
+        v["frac"] = v["achieved_gbs"] / hbm_peak
+    return res
+
+
+@torch.inference_mode()
+def cpu_baseline_layer(engine, batch, step_idx, layers_total, threads=None):
+    """Oracle decode of ONE decoder layer for the whole batch on the host cores, scaled
+    to the full model (+ the LM head on a 16-row sample, scaled)."""
+    from oracle import fp8_decoder as O
+    runner = engine.runner
+    model = runner.model
+    layer = model.model.layers[0]
+    a = layer.self_attn
+    if threads:
+        torch.set_num_threads(threads)
+    B = batch["ids0"].shape[0]
+
+    def wp(lin):
+        return lin.weight_fp8.cpu(), lin.weight_scale.cpu()
+    lw = O.LayerWeights(wp(a.qkv_proj), wp(a.o_proj), wp(layer.mlp.gate_up_proj), wp(layer.mlp.down_proj),
+                        layer.input_layernorm.weight.cpu(), layer.post_attention_layernorm.weight.cpu(),
+                        a.q_norm.weight.cpu(), a.k_norm.weight.cpu())
+    bt = batch["bt"].cpu()
+    used = sorted({int(b) for b in bt.flatten().tolist() if b >= 0})
+    remap = {b: i for i, b in enumerate(used)}
+    bt_local = bt.clone().apply_(lambda b: remap.get(b, -1))
+    caches = [a.attn.k_cache[used].cpu(), a.attn.v_cache[used].cpu(), a.attn.k_scale_cache[used].cpu(),
+              a.attn.v_scale_cache[used].cpu()]
+    pos = batch["pos"][step_idx].cpu()
+    slots = (bt_local.gather(1, (pos // BLOCK).unsqueeze(1)).squeeze(1).long() * BLOCK + pos % BLOCK)
+    cos, sin = O.rope_tables(HEAD_DIM, int(pos.max()) + 1, 1e6)
+    hidden = torch.randn(B, model.config.hidden_size, dtype=torch.float16)
+    residual = torch.randn_like(hidden)
+    t0 = time.perf_counter()
+    O.decoder_layer(lw, pos, hidden, residual, Hq=a.num_heads, Hkv=a.num_kv_heads, D=HEAD_DIM, eps=1e-6,
+                    cos_cache=cos, sin_cache=sin, mode="decode", caches=caches, slots=slots,
+                    seqlens=(pos + 1), block_tables=bt_local)
+    t_layer = time.perf_counter() - t0
+    head = model.lm_head.weight.cpu()
+    t1 = time.perf_counter()
+    (hidden[:16].float() @ head.float().T).half()
+    t_head = (time.perf_counter() - t1) * B / 16
+    per_step = t_layer * layers_total + t_head
+    return dict(value=B / per_step, unit="tok/s", cores=torch.get_num_threads(), kind="port",
+                sample=f"1 of {layers_total} decoder layers of one B={B} decode step (+ LM head on 16 rows), "
+                       f"scaled to the full model; oracle/fp8_decoder.py on {torch.get_num_threads()} threads",
+                seconds_sampled=t_layer + (time.perf_counter() - t1))
+
+
+def run_ours(args):
+    from microserve_b200 import _lib
+    from microserve_b200.utils import dist as tp
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+        tp.init_tensor_parallel()
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    lib = _lib.load()
+    cfg = qwen3_cfg(args.model)
+    reqs = prompts(args.batch, args.prompt_min, args.prompt_max, cfg.vocab_size)
+    steps_total = args.warmup + args.steps
+    max_len = args.prompt_max + max(args.output_len, steps_total) + 2 * BLOCK
+    engine = build_engine(args, cfg, max_len)
+    hbm_peak, peak_kind = peaks()
+
+    result = {}
+    if not args.no_e2e:
+        # warm-up job (short), then the timed full job
+        run_e2e(engine, reqs, 4)
+        e2e_tps, itl, e2e_s, h2d, d2h, e2e_steps = run_e2e(engine, reqs, args.output_len)
+        result["e2e"] = {"value": round(e2e_tps, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
+                         "d2h_bytes_per_step": int(d2h), "itl_p50_ms": itl, "elapsed_s": round(e2e_s, 3),
+                         "engine_steps": e2e_steps, "output_tokens": args.batch * args.output_len}
+
+    batch = prepare_decode_batch(engine, reqs, steps_total)
+    step = decode_step_runner(engine, batch)
+    launches_before = lib.ms_launch_count()
+    for i in range(args.warmup):
+        step(i)
+    sync_all()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for i in range(args.warmup, steps_total):
+            step(i)
+        end.record()
+        torch.cuda.synchronize()
+    elapsed = max_over_ranks(start.elapsed_time(end) / 1e3)
+    assert lib.ms_launch_count() == launches_before, "graph replay must not call the library"
+    B = args.batch
+    value = B * args.steps / elapsed
+    ms_step = elapsed / args.steps * 1e3
+
+    kern = kernel_rooflines(engine, batch, args.warmup, hbm_peak)
+    L = cfg.num_hidden_layers
+    dominant = max(kern, key=lambda k: kern[k]["seconds"] * kern[k]["per_layer"])
+    d = kern[dominant]
+    status = _lib.device_status()
+
+    # algorithmic bytes of the whole decode step (per GPU) for context
+    ctx = batch["lens"][args.warmup].double().sum().item()
+    w_layers = sum(m.weight_fp8.numel() for m in engine.runner.model.modules() if hasattr(m, "weight_fp8"))
+    kv_bytes = ctx * L * cfg.num_key_value_heads // args.gpus * (2 * HEAD_DIM + 8)
+    head_bytes = engine.runner.model.lm_head.weight.numel() * 2
+    step_bytes = w_layers + kv_bytes + head_bytes
+
+    line = {
+        "metric": "output tok/s Qwen3-8B FP8 decode (FP8 KV), batch 256",
+        "value": round(value, 1), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 acc, f16 activations",
+        "data": "synthetic: random N(0,0.02) weights quantised to FP8, prompts U[128,1024] from random.Random(0)",
+        "config": {"workload": f"Qwen3-{args.model.upper()}-shaped decode step, batch {B}, contexts "
+                               f"{int(batch['ctx0'].min())}-{int(batch['ctx0'].max())} growing 1 token/step",
+                   "model": f"qwen3-{args.model}", "global_batch": B, "seq_len": int(batch["ctx0"].mean()),
+                   "parallelism": f"tp{args.gpus}", "kv_cache": "fp8_e4m3, 256-token pages",
+                   "l2": "inputs larger than L2 (weights + KV >> 126 MB); no flush"},
+        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(d["achieved_gbs"], 1),
+                     "peak": hbm_peak, "unit": "GB/s", "frac": round(d["frac"], 4), "traffic": None,
+                     "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s"},
+        "kernels": {k: {"us": round(v["seconds"] * 1e6, 2), "GBps": round(v["achieved_gbs"], 1),
+                        "frac": round(v["frac"], 4)} for k, v in kern.items()},
+        "step_roofline": {"algorithmic_bytes": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
+                          "frac": round(step_bytes / (ms_step / 1e3) / 1e9 / hbm_peak, 4)},
+        "gpu_launches": int(engine.runner.kernels_per_decode_step.get(B, 0)) * args.steps,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    line.update(result)
+    if rank == 0 and args.gpus == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_layer(engine, batch, args.warmup, L)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    engine.runner.release_graphs()
+    if torch.distributed.is_initialized():
+        torch.distributed.destroy_process_group()
+
+
+# ------------------------------------------------------------------------ reference
+def run_reference(args):
+    """The reference path restated on the CPU (oracle), on this box's host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import fp8_decoder as O
+    m = MODELS[args.model]
+    torch.manual_seed(0)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    H, I, Hq, Hkv, L, V = m["hidden"], m["inter"], m["heads"], m["kv_heads"], m["layers"], m["vocab"]
+
+    def lin(n, k):
+        return O.quantize_weight((torch.randn(n, k) * 0.02).half())
+    lw = O.LayerWeights(lin((Hq + 2 * Hkv) * HEAD_DIM, H), lin(H, Hq * HEAD_DIM), lin(2 * I, H), lin(H, I),
+                        torch.ones(H).half(), torch.ones(H).half(), torch.ones(HEAD_DIM).half(),
+                        torch.ones(HEAD_DIM).half())
+    reqs_lens = [len(p) for p in prompts(args.batch, args.prompt_min, args.prompt_max, 1000)]
+    B = args.batch
+    nblk = [(c + 1 + args.steps + args.warmup) // BLOCK + 1 for c in reqs_lens]
+    tot = sum(nblk)
+    kc = torch.randint(0, 120, (tot, BLOCK, Hkv, HEAD_DIM), dtype=torch.uint8).view(torch.float8_e4m3fn)
+    vc = torch.randint(0, 120, (tot, BLOCK, Hkv, HEAD_DIM), dtype=torch.uint8).view(torch.float8_e4m3fn)
+    ks = torch.rand(tot, BLOCK, Hkv) * 1e-3
+    vs = torch.rand(tot, BLOCK, Hkv) * 1e-3
+    tables, o = [], 0
+    for n in nblk:
+        tables.append(list(range(o, o + n)))
+        o += n
+    bt = O.block_table_rows(tables)
+    head = (torch.randn(V, H) * 0.02).half()
+    cos, sin = O.rope_tables(HEAD_DIM, args.prompt_max + args.steps + args.warmup + 2, 1e6)
+    times = []
+    for it in range(args.warmup + args.steps):
+        pos = torch.tensor([c + it for c in reqs_lens])
+        slots = torch.tensor([tables[b][p // BLOCK] * BLOCK + p % BLOCK for b, p in enumerate(pos.tolist())])
+        hidden = torch.randn(B, H).half()
+        t0 = time.perf_counter()
+        O.decoder_layer(lw, pos, hidden, torch.randn(B, H).half(), Hq=Hq, Hkv=Hkv, D=HEAD_DIM, eps=1e-6,
+                        cos_cache=cos, sin_cache=sin, mode="decode", caches=[kc, vc, ks, vs], slots=slots,
+                        seqlens=pos + 1, block_tables=bt)
+        t_layer = time.perf_counter() - t0
+        t1 = time.perf_counter()
+        (hidden[:16].float() @ head.float().T).half()
+        t_head = (time.perf_counter() - t1) * B / 16
+        if it >= args.warmup:
+            times.append(t_layer * L + t_head)
+    per_step = statistics.mean(times)
+    value = B / per_step
+    sample = (f"1 of {L} decoder layers of a B={B} decode step (+ LM head on 16 rows) per step, scaled to the "
+              f"full model; oracle/fp8_decoder.py (torch CPU) on {threads} threads")
+    line = {"impl": "reference", "metric": "output tok/s Qwen3-8B FP8 decode (FP8 KV), batch 256",
+            "value": round(value, 3), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 2), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (CPU fp32 math)",
+            "data": "synthetic", "config": {"workload": f"Qwen3-{args.model.upper()}-shaped decode step, batch {B}",
+                                            "model": f"qwen3-{args.model}", "global_batch": B,
+                                            "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", choices=sorted(MODELS), default="8b")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--prompt-min", type=int, default=128)
+    ap.add_argument("--prompt-max", type=int, default=1024)
+    ap.add_argument("--output-len", type=int, default=512)
+    ap.add_argument("--max-batched-tokens", type=int, default=8192)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

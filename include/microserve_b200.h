@@ -41,6 +41,11 @@ int ms_version(void);
 /* Message for the last non-zero return code on this thread. */
 const char* ms_last_error(void);
 
+/* Number of kernel launches the library has issued from this process (host
+ * counter; a CUDA-graph replay re-runs captured launches without calling the
+ * library, so it is counted once, at capture). */
+int64_t ms_launch_count(void);
+
 /* Reads and clears the device status word of the current device. Kernels
  * that wait on barriers give up after a bounded time, record a non-zero code
  * there (1 = tensor-core pipeline timeout, 2 = peer timeout) and return.

@@ -53,6 +53,8 @@ int ms_version(void) { return 100; }
 
 const char* ms_last_error(void) { return g_err.c_str(); }
 
+int64_t ms_launch_count(void) { return ms::g_host_launches.load(std::memory_order_relaxed); }
+
 int ms_get_device_status(int* status, void* stream) {
   if (status == nullptr) return fail(MS_ERR_INVALID, "ms_get_device_status: status is NULL");
   int host = 0, zero = 0;

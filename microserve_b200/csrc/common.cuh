@@ -14,6 +14,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #define MS_FP8_MAX 448.0f
 
 namespace ms {
@@ -30,6 +32,12 @@ enum DeviceStatus : int {
 };
 
 extern __device__ int g_device_status;
+
+// Host-side count of kernel launches issued by the library (for launch
+// accounting in benchmarks; a CUDA-graph replay re-runs captured launches
+// without counting them again).
+extern std::atomic<long long> g_host_launches;
+#define MS_COUNT_LAUNCH() (::ms::g_host_launches.fetch_add(1, std::memory_order_relaxed))
 
 __device__ __forceinline__ void set_device_status(int code) {
   atomicCAS(&g_device_status, 0, code);

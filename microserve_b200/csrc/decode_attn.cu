@@ -16,10 +16,13 @@
 //    The head_dim axis of each product is permuted so that every thread's
 //    fragment comes from contiguous bytes it loaded itself; Q and O use the
 //    same permutation, so results are unchanged. The per-token k scale is
-//    applied to the fp32 scores; the per-token v scale is folded into P'
-//    (P' = p * v_scale) before it is rounded to f16 for the second product.
-//    P' changes from the accumulator layout to the operand layout with
-//    movmatrix (an in-register 8x8 transpose).
+//    applied to the fp32 scores; the per-token v scale is folded into the
+//    exponent (P' = exp2(s + log2(v_scale) - m), all weights in (0, 1]) and
+//    P' enters the second product as two f16 parts (hi + lo), so the result
+//    keeps fp32-level accuracy like the reference's all-fp32 kernel: FP8
+//    activation quantisation downstream turns fp16-level attention errors
+//    into visible output differences. P' changes from the accumulator layout
+//    to the operand layout with movmatrix (an in-register 8x8 transpose).
 //  * Online softmax in the exp2 domain; warps of a CTA interleave 16-token
 //    tiles and are merged through shared memory at the end. Long contexts with
 //    few sequences are split over CTAs (flash-decoding); partial (m, l, o)
@@ -33,6 +36,8 @@ namespace {
 constexpr int kD = 128;
 constexpr int kWarps = 4;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kPScaleLog2 = 14.f;       // P' scaled into [0, 2^14] for its f16 hi/lo split
+constexpr float kPUnscale = 1.f / 16384.f;
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -55,9 +60,21 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   return y;
 }
 
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float2 h2_to_f2(uint32_t x) {
+  __half2 h;
+  memcpy(&h, &x, 4);
+  return __half22float2(h);
 }
 
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
@@ -169,7 +186,12 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(DecodeArgs a) {
     s[2] = ok1 ? s[2] * ks1 * a.scale_log2 : -INFINITY;
     s[3] = ok1 ? s[3] * ks1 * a.scale_log2 : -INFINITY;
 
-    float tmax0 = fmaxf(s[0], s[2]), tmax1 = fmaxf(s[1], s[3]);
+    // Fold the per-token v scale into the exponent: w = p * v_scale = exp2(s + log2(v_scale) - m),
+    // with the running max m taken over s + log2(v_scale), so every weight is in (0, 1] and its
+    // f16 hi/lo split (below) keeps ~22 bits. The denominator sums exp2(s - m) in fp32.
+    const float lv0 = lg2(vs0), lv1 = lg2(vs1);
+    const float w0 = s[0] + lv0, w1 = s[1] + lv0, w2 = s[2] + lv1, w3 = s[3] + lv1;
+    float tmax0 = fmaxf(w0, w2), tmax1 = fmaxf(w1, w3);
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
       tmax0 = fmaxf(tmax0, __shfl_xor_sync(0xffffffffu, tmax0, o));
@@ -180,20 +202,23 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(DecodeArgs a) {
     const float al0 = ex2(m_run[0] - mn0), al1 = ex2(m_run[1] - mn1);
     m_run[0] = mn0;
     m_run[1] = mn1;
-    const float p00 = ex2(s[0] - mn0), p01 = ex2(s[1] - mn1);
-    const float p10 = ex2(s[2] - mn0), p11 = ex2(s[3] - mn1);
-    l_run[0] = l_run[0] * al0 + p00 + p10;
-    l_run[1] = l_run[1] * al1 + p01 + p11;
+    l_run[0] = l_run[0] * al0 + ex2(s[0] - mn0) + ex2(s[2] - mn0);
+    l_run[1] = l_run[1] * al1 + ex2(s[1] - mn1) + ex2(s[3] - mn1);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       acc[i][0] *= al0; acc[i][1] *= al1;
       acc[i][2] *= al0; acc[i][3] *= al1;
     }
-    // P'^T operand: fold the per-token v scale, round to f16, transpose.
-    const uint32_t x0 = pack_h2(p00 * vs0, p01 * vs0);
-    const uint32_t x1 = pack_h2(p10 * vs1, p11 * vs1);
-    const uint32_t pb0 = movmatrix_trans(x0);
-    const uint32_t pb1 = movmatrix_trans(x1);
+    // P'^T operand, as f16 hi + lo parts, transposed to the B layout. The weights are
+    // scaled by 2^kPScaleLog2 (undone in the final division) so that lo stays a normal
+    // f16 for every weight that matters (P' >= 2^-16).
+    const float q00 = ex2(w0 - mn0 + kPScaleLog2), q01 = ex2(w1 - mn1 + kPScaleLog2);
+    const float q10 = ex2(w2 - mn0 + kPScaleLog2), q11 = ex2(w3 - mn1 + kPScaleLog2);
+    const uint32_t h0 = pack_h2(q00, q01), h1 = pack_h2(q10, q11);
+    const float2 h0f = h2_to_f2(h0), h1f = h2_to_f2(h1);
+    const uint32_t l0 = pack_h2(q00 - h0f.x, q01 - h0f.y), l1 = pack_h2(q10 - h1f.x, q11 - h1f.y);
+    const uint32_t pb0 = movmatrix_trans(h0), pb1 = movmatrix_trans(h1);
+    const uint32_t pc0 = movmatrix_trans(l0), pc1 = movmatrix_trans(l1);
 
     // ---- O^T += V^T . P'^T ---------------------------------------------
     const uint32_t va[4] = {v0.x, v0.y, v0.z, v0.w};
@@ -212,6 +237,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(DecodeArgs a) {
       const uint32_t a2 = e4m3x2_to_f16x2((uint16_t)(hi & 0xffff));
       const uint32_t a3 = e4m3x2_to_f16x2((uint16_t)(hi >> 16));
       mma16816(acc[i], a0, a1, a2, a3, pb0, pb1);
+      mma16816(acc[i], a0, a1, a2, a3, pc0, pc1);
     }
   }
 
@@ -256,7 +282,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(DecodeArgs a) {
     }
     const int hq = kvh * G + h;
     if (a.splits == 1) {
-      const float inv = (L > 0 && Lsum > 0.f) ? 1.f / Lsum : 0.f;
+      const float inv = (L > 0 && Lsum > 0.f) ? kPUnscale / Lsum : 0.f;
       uint4 packed;
       packed.x = pack_h2(o[0] * inv, o[1] * inv);
       packed.y = pack_h2(o[2] * inv, o[3] * inv);
@@ -292,7 +318,7 @@ __global__ void __launch_bounds__(kD) decode_merge_kernel(const float* __restric
     Lsum += ws_ml[(row0 + s) * 2 + 1] * wt;
     o += ws_o[(row0 + s) * kD + d] * wt;
   }
-  const float r = (seqlens[b] > 0 && Lsum > 0.f) ? o / Lsum : 0.f;
+  const float r = (seqlens[b] > 0 && Lsum > 0.f) ? o * kPUnscale / Lsum : 0.f;
   out[((int64_t)b * Hq + hq) * kD + d] = __float2half_rn(r);
 }
 
@@ -341,9 +367,11 @@ cudaError_t launch_decode_attention(const void* q, const void* k_cache, const vo
   a.scale_log2 = softmax_scale * kLog2e;
   dim3 grid(splits, Hkv, B);
   decode_kernel<<<grid, kWarps * 32, 0, stream>>>(a);
+  MS_COUNT_LAUNCH();
   if (splits > 1) {
     dim3 g2(Hq, B);
     decode_merge_kernel<<<g2, kD, 0, stream>>>(a.ws_o, a.ws_ml, seqlens, Hq, splits, (__half*)out);
+    MS_COUNT_LAUNCH();
   }
   return cudaGetLastError();
 }

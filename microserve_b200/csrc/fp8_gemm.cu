@@ -348,6 +348,7 @@ cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const GemmAr
     attr_set = true;
   }
   fp8_gemm_kernel<BN><<<grid, kThreads, C::kSmemBytes, stream>>>(mw, mx, args);
+  MS_COUNT_LAUNCH();
   return cudaGetLastError();
 }
 
@@ -393,6 +394,7 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
     dim3 grid((N + 127) / 128, M);
     fp8_gemm_simt_kernel<<<grid, 128, 0, stream>>>((const uint8_t*)xq, (const uint8_t*)wq, M, N, K, sx, sw,
                                                     (const __half*)bias, (__half*)y);
+    MS_COUNT_LAUNCH();
     return cudaGetLastError();
   }
   int bn, splits;
@@ -426,6 +428,7 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   if (blocks > num_sms * 8) blocks = num_sms * 8;
   splitk_reduce_kernel<<<blocks, 256, 0, stream>>>((const float*)workspace, splits, M, N, sx, sw,
                                                     (const __half*)bias, (__half*)y);
+  MS_COUNT_LAUNCH();
   return cudaGetLastError();
 }
 

@@ -162,6 +162,7 @@ cudaError_t launch_store_kv_fp8(const void* k, const void* v, int64_t T, int kv_
   const int64_t items = T * kv_heads;
   store_kv_fp8_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream>>>(
       (const __half*)k, (const __half*)v, T, kv_heads, slots, (uint8_t*)k_cache, (uint8_t*)v_cache, k_scale, v_scale);
+  MS_COUNT_LAUNCH();
   return cudaGetLastError();
 }
 
@@ -193,6 +194,7 @@ cudaError_t launch_qkv_post(const void* qkv, int64_t T, int q_heads, int kv_head
   const int heads = q_heads + 2 * kv_heads;
   dim3 grid((unsigned)T, (unsigned)((heads + 7) / 8));
   qkv_post_kernel<<<grid, 256, 0, stream>>>(a);
+  MS_COUNT_LAUNCH();
   return cudaGetLastError();
 }
 

@@ -343,6 +343,7 @@ cudaError_t launch_prefill_attention(bool paged, const void* q, const void* k16,
     prefill_kernel<true><<<grid, 128, 0, stream>>>(a);
   else
     prefill_kernel<false><<<grid, 128, 0, stream>>>(a);
+  MS_COUNT_LAUNCH();
   return cudaGetLastError();
 }
 

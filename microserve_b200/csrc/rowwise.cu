@@ -193,11 +193,13 @@ cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t M, int K, v
       cudaFuncSetAttribute(quantize_rows_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     quantize_rows_kernel<true><<<(unsigned)M, row_threads(K), smem, stream>>>((const __half*)x, ldx, K,
                                                                               (uint8_t*)xq, sx);
+    MS_COUNT_LAUNCH();
   } else {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(quantize_rows_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     quantize_rows_kernel<false><<<(unsigned)M, row_threads(K), smem, stream>>>((const __half*)x, ldx, K,
                                                                                (uint8_t*)xq, sx);
+    MS_COUNT_LAUNCH();
   }
   return cudaGetLastError();
 }
@@ -212,6 +214,7 @@ cudaError_t launch_rmsnorm(const void* x, const void* residual, const void* weig
   rmsnorm_kernel<<<(unsigned)M, row_threads(H), smem, stream>>>(
       (const __half*)x, (const __half*)residual, (const __half*)weight, H, eps, (__half*)residual_out, (__half*)y,
       (uint8_t*)yq, sy);
+  MS_COUNT_LAUNCH();
   return cudaGetLastError();
 }
 
@@ -223,6 +226,7 @@ cudaError_t launch_silu_mul(const void* gu, int64_t M, int I, void* out, void* a
     cudaFuncSetAttribute(silu_mul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   silu_mul_kernel<<<(unsigned)M, row_threads(I), smem, stream>>>((const __half*)gu, I, (__half*)out,
                                                                   (uint8_t*)aq, sa);
+  MS_COUNT_LAUNCH();
   return cudaGetLastError();
 }
 

@@ -3,4 +3,5 @@
 
 namespace ms {
 __device__ int g_device_status = 0;
+std::atomic<long long> g_host_launches{0};
 }  // namespace ms

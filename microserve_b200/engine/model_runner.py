@@ -46,6 +46,7 @@ class _HostBatch:
         self.device = device
         self.host = torch.empty(0, dtype=torch.uint8).pin_memory()
         self.dev = torch.empty(0, dtype=torch.uint8, device=device)
+        self.bytes_uploaded = 0
 
     def upload(self, arrays: list[np.ndarray]) -> list[torch.Tensor]:
         offs, total = [], 0
@@ -63,6 +64,7 @@ class _HostBatch:
         dev = torch.empty(total, dtype=torch.uint8, device=self.device)
         dev.copy_(self.host[:total], non_blocking=True)
         self.dev = dev
+        self.bytes_uploaded += total
         out = []
         for a, o in zip(arrays, offs):
             t = dev[o:o + a.nbytes].view(torch.int64 if a.dtype == np.int64 else torch.int32)
@@ -130,6 +132,7 @@ class ModelRunner:
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_pool = None
         self.graph_vars: dict | None = None
+        self.kernels_per_decode_step: dict[int, int] = {}  # library launches captured per graph
         if not self.enforce_eager:
             self._warmup()
             self._capture_decode_graphs()
@@ -390,6 +393,8 @@ class ModelRunner:
         )
         self.graph_vars = gv
         self._reserve_workspace(max_bs, max_blocks)
+        from microserve_b200 import _lib
+        lib = _lib.load()
 
         def body(bs):
             h = self.model(gv["input_ids"][:bs], gv["positions"][:bs])
@@ -404,8 +409,10 @@ class ModelRunner:
             body(bs)  # eager run: sets kernel attributes, tensor maps, allocator state
             torch.cuda.synchronize()
             graph = torch.cuda.CUDAGraph()
+            n0 = lib.ms_launch_count()
             with torch.cuda.graph(graph, pool=self.graph_pool):
                 body(bs)
+            self.kernels_per_decode_step[bs] = lib.ms_launch_count() - n0
             if self.graph_pool is None:
                 self.graph_pool = graph.pool()
             self.graphs[bs] = graph

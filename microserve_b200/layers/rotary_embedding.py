@@ -21,8 +21,11 @@ class RotaryEmbedding(nn.Module):
         super().__init__()
         self.head_size = head_size
         assert rotary_dim == head_size
-        inv_freq = 1.0 / (base ** (torch.arange(0, rotary_dim, 2, dtype=torch.float32) / rotary_dim))
-        t = torch.arange(max_position_embeddings, dtype=torch.float32)
+        # built on the host even when the model is constructed under a CUDA device context,
+        # so the tables are the reference's CPU-computed values
+        cpu = torch.device("cpu")
+        inv_freq = 1.0 / (base ** (torch.arange(0, rotary_dim, 2, dtype=torch.float32, device=cpu) / rotary_dim))
+        t = torch.arange(max_position_embeddings, dtype=torch.float32, device=cpu)
         freqs = torch.einsum("i,j -> ij", t, inv_freq)
         emb = torch.cat((freqs, freqs), dim=-1)
         cos = emb.cos().unsqueeze_(1)

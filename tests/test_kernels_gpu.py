@@ -236,6 +236,37 @@ def _fill_cache(lengths, tables, hkv=HKV, nb=None, seed=1, scale=0.2):
     return caches
 
 
+@pytest.mark.parametrize("lengths,hq,hkv,tables", [
+    ([38, 301, 514], 16, 8, [[0], [1, 2], [3, 4, 5]]),
+    ([301, 701], 16, 8, [[0, 1], [2, 3, 4]]),
+    ([600, 900, 3], 32, 8, [[5, 1, 0], [2, 3, 4, 6], [7]]),
+])
+def test_decode_attention_fixed_tables(lengths, hq, hkv, tables):
+    from microserve_b200.layers.fp8_decode_attention import fp8_decode_attention
+    caches = _fill_cache(lengths, tables, hkv=hkv, seed=13, scale=0.8)
+    bt = O.block_table_rows(tables)
+    torch.manual_seed(10)
+    q = torch.randn(len(lengths), hq, D, dtype=torch.float16)
+    got = fp8_decode_attention(q.cuda(), *[c.cuda() for c in caches], torch.tensor(lengths, dtype=torch.int32).cuda(),
+                               bt.cuda(), D ** -0.5).cpu()
+    ref = O.decode_attention(q, *caches, torch.tensor(lengths), bt, D ** -0.5)
+    for b in range(len(lengths)):
+        assert O.rel_l2(got[b], ref[b]) < 1e-3, (b, O.rel_l2(got[b], ref[b]))
+    # fp32-level accuracy (the reference decode kernel is all-fp32): against an fp64
+    # evaluation, outputs are the correctly rounded fp16 value or 1 ulp off, rarely.
+    head_map = torch.arange(hq) // (hq // hkv)
+    for b, L in enumerate(lengths):
+        kk = O.gather_kv(caches[0], caches[2], bt[b], L)[:, head_map].double()
+        vv = O.gather_kv(caches[1], caches[3], bt[b], L)[:, head_map].double()
+        sc = torch.einsum("hd,lhd->hl", q[b].double(), kk) * D ** -0.5
+        exact = torch.einsum("hl,lhd->hd", sc.softmax(-1), vv)
+        rounded = exact.half()
+        ulp = (rounded.float().abs() * 2.0 ** -10).clamp_min(2.0 ** -24)
+        err = (got[b].float() - exact.float()).abs()
+        assert (err <= ulp).all(), (b, (err / ulp).max().item())
+        assert (got[b] != rounded).float().mean().item() < 0.02, (b, (got[b] != rounded).float().mean().item())
+
+
 @pytest.mark.parametrize("lengths,hq,hkv", [
     ([1, 73, 300], 16, 8),            # tests/test_fp8_kv_attention.py:39-73
     ([0, 5, 256, 257, 1000], 32, 8),  # empty row, page edges
