@@ -131,7 +131,8 @@ def build_engine(args, cfg, max_model_len):
     return LLMEngine(Config(hf_config=cfg, load_format="dummy", quantization="fp8_dynamic",
                             kv_cache_dtype="fp8_e4m3", max_num_seqs=args.batch,
                             max_num_batched_tokens=args.max_batched_tokens, max_model_len=max_model_len,
-                            tensor_parallel_size=args.gpus, gpu_memory_utilization=0.9, seed=0))
+                            tensor_parallel_size=args.gpus, gpu_memory_utilization=0.9, seed=0,
+                            num_kvcache_blocks=args.kv_blocks))
 
 
 def sync_all():
@@ -228,13 +229,20 @@ def decode_step_runner(engine, batch):
 
 
 def time_kernel(fn, iters=20, warm=3):
+    """Device time of one fn() call: `iters` calls captured in a CUDA graph and
+    replayed (so host launch overhead is not measured), CUDA events around the replay."""
     for _ in range(warm):
         fn()
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(iters):
+            fn()
+    graph.replay()  # warm the graph itself
+    torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for _ in range(iters):
-        fn()
+    graph.replay()
     e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / 1e3 / iters
@@ -360,11 +368,13 @@ def run_ours(args):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        torch.cuda.nvtx.range_push("decode_timed")
         start.record()
         for i in range(args.warmup, steps_total):
             step(i)
         end.record()
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     elapsed = max_over_ranks(start.elapsed_time(end) / 1e3)
     assert lib.ms_launch_count() == launches_before, "graph replay must not call the library"
     B = args.batch
@@ -482,6 +492,74 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+@torch.inference_mode()
+def run_kernel(args):
+    """One kernel on synthetic inputs of a Qwen3 layer's shapes, timed with CUDA events
+    (used for the kernel sweeps of BASELINE config 5 and for ncu captures). One JSON line
+    per case."""
+    from microserve_b200 import _lib, kernels
+    from oracle import fp8_decoder as O
+    _lib.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    m = MODELS[args.model]
+    hbm_peak, _ = peaks()
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.kernel == "decode_attention":
+        Hq, Hkv = m["heads"] // args.gpus, m["kv_heads"] // args.gpus
+        for ctx in [int(c) for c in args.ctx.split(",")]:
+            B = args.batch
+            nb = (ctx + BLOCK - 1) // BLOCK
+            blocks = B * nb
+            kc = torch.randint(0, 120, (blocks + 1, BLOCK, Hkv, HEAD_DIM), dtype=torch.uint8, device=dev,
+                               generator=g).view(torch.float8_e4m3fn)
+            vc = torch.randint(0, 120, (blocks + 1, BLOCK, Hkv, HEAD_DIM), dtype=torch.uint8, device=dev,
+                               generator=g).view(torch.float8_e4m3fn)
+            ks = torch.rand(blocks + 1, BLOCK, Hkv, device=dev, generator=g) * 1e-2 + 1e-3
+            vs = torch.rand(blocks + 1, BLOCK, Hkv, device=dev, generator=g) * 1e-2 + 1e-3
+            perm = torch.randperm(blocks, device=dev, generator=g).to(torch.int32)
+            bt = perm.view(B, nb)
+            lens = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+            q = torch.randn(B, Hq, HEAD_DIM, device=dev, dtype=torch.float16, generator=g)
+            out = torch.empty_like(q)
+            t = time_kernel(lambda: kernels.paged_decode_fp8(q, kc, vc, ks, vs, lens, bt, HEAD_DIM ** -0.5, out=out),
+                            iters=args.steps, warm=args.warmup)
+            byts = B * ctx * Hkv * (2 * HEAD_DIM + 8) + 2 * B * Hq * HEAD_DIM * 2 + B * (4 + 4 * nb)
+            print(json.dumps({"kernel": "decode_attention", "model": args.model, "tp": args.gpus, "batch": B,
+                              "ctx": ctx, "q_heads": Hq, "kv_heads": Hkv, "us": round(t * 1e6, 2),
+                              "bytes": byts, "GBps": round(byts / t / 1e9, 1),
+                              "frac_hbm": round(byts / t / 1e9 / hbm_peak, 4)}), flush=True)
+            del kc, vc, ks, vs
+    else:
+        if args.shapes:
+            shapes = [tuple(int(x) for x in sh.split(":")) for sh in args.shapes.split(",")]
+        else:
+            H, I, Hq, Hkv = m["hidden"], m["inter"], m["heads"], m["kv_heads"]
+            t_ = args.gpus
+            shapes = [(args.batch, (Hq + 2 * Hkv) * HEAD_DIM // t_, H), (args.batch, H, Hq * HEAD_DIM // t_),
+                      (args.batch, 2 * I // t_, H), (args.batch, H, I // t_)]
+        for (M, N, K) in shapes:
+            xq, sx = O.quantize_rows(torch.randn(M, K).half())
+            # enough weight copies that consecutive launches never find their weights in L2
+            copies = max(2, -(-256 * 2 ** 20 // (N * K)))
+            wqs = [torch.randint(0, 120, (N, K), dtype=torch.uint8, device=dev, generator=g).view(torch.float8_e4m3fn)
+                   for _ in range(copies)]
+            sw = torch.rand(N, device=dev, generator=g) * 1e-3
+            xq, sx = xq.to(dev), sx.to(dev)
+            y = torch.empty(M, N, device=dev, dtype=torch.float16)
+            it = [0]
+
+            def launch():
+                kernels.fp8_gemm(xq, sx, wqs[it[0] % copies], sw, out=y)
+                it[0] += 1
+            t = time_kernel(launch, iters=args.steps, warm=args.warmup)
+            byts = N * K + M * K + 2 * M * N + 4 * (M + N)
+            flops = 2 * M * N * K
+            print(json.dumps({"kernel": "fp8_gemm", "M": M, "N": N, "K": K, "us": round(t * 1e6, 2),
+                              "GBps": round(byts / t / 1e9, 1), "frac_hbm": round(byts / t / 1e9 / hbm_peak, 4),
+                              "TFLOPs": round(flops / t / 1e12, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -496,10 +574,18 @@ def main():
     ap.add_argument("--max-batched-tokens", type=int, default=8192)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kv-blocks", type=int, default=0, help="KV-cache blocks (0: size from free memory)")
+    ap.add_argument("--kernel", choices=["decode_attention", "gemm"], default=None,
+                    help="time one kernel on synthetic inputs (sweeps / profiling) instead of the model")
+    ap.add_argument("--ctx", type=str, default="832", help="--kernel decode_attention: context lengths, comma list")
+    ap.add_argument("--shapes", type=str, default="",
+                    help="--kernel gemm: M:N:K comma list (default: the 8B layer's four linears at M=--batch)")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
     if args.impl == "reference":
         run_reference(args)
+    elif args.kernel is not None:
+        run_kernel(args)
     else:
         run_ours(args)
 

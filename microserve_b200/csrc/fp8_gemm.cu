@@ -17,8 +17,10 @@
 // shared-memory stages; warp 1 owns the TMEM accumulator and issues
 // tcgen05.mma (kind::f8f6f4, 128 x BN x 32 per instruction, 4 per 128-byte K
 // step); warps 2-5 drain TMEM with tcgen05.ld and apply the dequant epilogue.
-// Small tile counts split K over CTAs: each split writes an fp32 partial and a
-// second kernel reduces the partials and applies the epilogue.
+// The kernel is persistent and stream-K scheduled: the tiles x K-steps work is
+// split evenly over at most one CTA per SM, and tiles shared by two CTAs are
+// summed in-kernel (fp32 partials in the caller's workspace), so there is no
+// wave quantisation and no separate reduction pass.
 //
 // Every wait is bounded (common.cuh: mbar_wait); on a timeout the kernel
 // records a device status, skips the rest and still frees its TMEM.
@@ -37,13 +39,18 @@ constexpr int kThreads = 192;  // 6 warps
 
 struct GemmArgs {
   int M, N, K;
-  int k_tiles_per_split;
-  int k_tiles;
+  int KT;       // K tiles of kBK bytes
+  int tiles_m;  // token tiles
+  int64_t T;    // output tiles
+  int64_t U;    // work units = tiles * KT
+  int G;        // CTAs (persistent, all co-resident)
+  int dp;       // 1: whole tiles round-robin (no K split); 0: stream-K
   const float* sx;
   const float* sw;
   const __half* bias;
   __half* y;
-  float* ws;  // split partials [splits, M, N] (splits > 1)
+  float* ws;   // [G][BN][kBM] fp32 partial tiles (stream-K fixup)
+  int* flags;  // [G] partial-ready flags; zero before and after every launch
 };
 
 template <int BN>
@@ -51,22 +58,25 @@ struct Cfg {
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = BN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : (BN >= 96 ? 7 : 8));
+  static constexpr int kAccCols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));  // TMEM columns
+  static constexpr int kTmemCols = 2 * kAccCols;  // two accumulators (double buffer)
+  static constexpr int kSxBytes = 2 * BN * 4;  // token scales of the current tile, double-buffered
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kSxBytes;
   // tcgen05 instruction descriptor: D=f32, A=B=e4m3, both K-major, N=BN, M=128.
   static constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with
 // 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart.
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   uint64_t d = 0;
-  d |= (uint64_t)((addr & 0x3FFFF) >> 4);         // start address
-  d |= (uint64_t)1 << 16;                           // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;                 // stride byte offset: 8 rows * 128 B
-  d |= (uint64_t)1 << 46;                           // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;                           // layout: SWIZZLE_128B
+  d |= (uint64_t)((addr & 0x3FFFF) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                   // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset: 8 rows * 128 B
+  d |= (uint64_t)1 << 46;                   // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                   // layout: SWIZZLE_128B
   return d;
 }
 
@@ -103,6 +113,64 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Epilogue warps only (4 warps, 128 threads): named barrier 1.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// First work unit of CTA c under the even partition of U units over G CTAs.
+__device__ __forceinline__ int64_t unit_begin(int64_t c, int64_t U, int G) { return c * U / G; }
+
+// The work of one CTA as a sequence of segments (tile t, K steps [kb, ke)).
+// Data-parallel mode: whole tiles cta, cta + G, ...; stream-K mode: the
+// CTA's contiguous range of the U = T * KT units, cut at tile boundaries.
+struct SegIter {
+  int64_t u, u_end, t_dp;
+  int64_t T;
+  int KT, G, dp;
+  __device__ SegIter(const GemmArgs& a, int cta)
+      : u(unit_begin(cta, a.U, a.G)), u_end(unit_begin(cta + 1, a.U, a.G)), t_dp(cta), T(a.T), KT(a.KT),
+        G(a.G), dp(a.dp) {}
+  __device__ bool next(int64_t& t, int& kb, int& ke) {
+    if (dp) {
+      if (t_dp >= T) return false;
+      t = t_dp;
+      kb = 0;
+      ke = KT;
+      t_dp += G;
+      return true;
+    }
+    if (u >= u_end) return false;
+    t = u / KT;
+    kb = (int)(u - t * KT);
+    ke = (int)((int64_t)KT < kb + (u_end - u) ? (int64_t)KT : kb + (u_end - u));
+    u += ke - kb;
+    return true;
+  }
+};
+
+// K-loop start offset of a whole-tile segment: different weight tiles begin at
+// different K so the CTAs of a wave spread their activation reads over L2.
+__device__ __forceinline__ int k_rotation(const GemmArgs& a, int64_t t, int kb, int ke) {
+  if (!a.dp || ke - kb < 2) return 0;
+  return (int)(((t / a.tiles_m) * 5) % (ke - kb));
+}
+
+// Stream-K persistent GEMM. The U = tiles * KT work units (one 128-byte K
+// step of one 128 x BN output tile) are split evenly over G co-resident CTAs;
+// each CTA walks its contiguous range tile by tile ("segments"). A segment
+// that starts at k = 0 owns its tile: when the tile continues in later CTAs,
+// the owner adds their fp32 partials (ws, flagged ready) before the epilogue.
+// A segment that starts mid-tile stores its partial and raises its flag.
+// The accumulator is double-buffered in TMEM so a tile's epilogue overlaps
+// the next tile's main loop.
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
@@ -114,25 +182,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
   uint64_t* empty = full + C::kStages;
-  uint64_t* done = empty + C::kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  __shared__ int s_abort;
+  uint64_t* acc_full = empty + C::kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* s_sx = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes + 256);  // [2][BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kBM;
-  const int m0 = blockIdx.y * BN;
-  const int split = blockIdx.z;
-  const int kt0 = split * args.k_tiles_per_split;
-  const int kt1 = min(args.k_tiles, kt0 + args.k_tiles_per_split);
-  const int nk = kt1 - kt0;
+  const int cta = blockIdx.x;
+  const int KT = args.KT;
 
   if (threadIdx.x == 0) {
-    s_abort = 0;
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
     fence_barrier_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_x) : "memory");
@@ -148,77 +215,169 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % C::kStages;
-        const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u)) {
-          s_abort = 1;
-          break;
+      int i = 0;  // stage counter across segments
+      SegIter it(args, cta);
+      int64_t t;
+      int kb, ke;
+      bool ok = true;
+      while (ok && it.next(t, kb, ke)) {
+        const int n0 = (int)(t / args.tiles_m) * kBM;
+        const int m0 = (int)(t % args.tiles_m) * BN;
+        const int nk = ke - kb, rot = k_rotation(args, t, kb, ke);
+        for (int j = 0; j < nk; ++j, ++i) {
+          const int s = i % C::kStages;
+          const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u)) {
+            ok = false;
+            break;
+          }
+          const int k = kb + (j + rot) % nk;
+          unsigned char* sa = smem + s * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+          tma_load_2d(&tmap_w, smem_u32(sa), &full[s], k * kBK, n0);
+          tma_load_2d(&tmap_x, smem_u32(sa + C::kABytes), &full[s], k * kBK, m0);
         }
-        unsigned char* sa = smem + s * C::kStageBytes;
-        mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-        const int kc = (kt0 + i) * kBK;
-        tma_load_2d(&tmap_w, smem_u32(sa), &full[s], kc, n0);
-        tma_load_2d(&tmap_x, smem_u32(sa + C::kABytes), &full[s], kc, m0);
       }
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      bool ok = true;
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % C::kStages;
-        const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
-        if (!mbar_wait(&full[s], ph)) {
-          ok = false;
-          s_abort = 1;
-          break;
-        }
+      int i = 0, seg = 0;
+      SegIter it(args, cta);
+      int64_t t;
+      int kb, ke;
+      while (it.next(t, kb, ke)) {
+        const int b = seg & 1;
+        if (!mbar_wait(&acc_empty[b], (((uint32_t)seg >> 1) & 1u) ^ 1u)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_addr = smem_u32(smem + s * C::kStageBytes);
-        const uint32_t b_addr = a_addr + C::kABytes;
+        const uint32_t acc = tmem + (uint32_t)(b * C::kAccCols);
+        bool ok = true;
+        for (int j = 0; j < ke - kb; ++j, ++i) {
+          const int s = i % C::kStages;
+          const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
+          if (!mbar_wait(&full[s], ph)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = smem_u32(smem + s * C::kStageBytes);
+          const uint32_t b_addr = a_addr + C::kABytes;
 #pragma unroll
-        for (int kk = 0; kk < kBK / 32; ++kk) {
-          umma_f8(tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), C::kIdesc,
-                  (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 32; ++kk) {
+            umma_f8(acc, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), C::kIdesc,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        if (!ok) break;
+        umma_commit(&acc_full[b]);
+        ++seg;
       }
-      if (ok) umma_commit(done);
     }
   } else {
-    // Epilogue warps 2..5 -> TMEM lane quarters 2,3,0,1.
+    // ---------------- epilogue (warps 2..5 -> TMEM lane quarters 2,3,0,1) ----------------
     const int q = warp & 3;
-    const int n = n0 + q * 32 + lane;
-    bool ok = (nk > 0) ? mbar_wait(done, 0) : true;
-    if (ok) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int row = q * 32 + lane;  // row within the 128-row weight tile
+    const int et = threadIdx.x - 64;
+    float* my_ws = args.ws + (int64_t)cta * BN * kBM;
+    int seg = -1;
+    SegIter it(args, cta);
+    int64_t t;
+    int kb, ke;
+    while (it.next(t, kb, ke)) {
+      ++seg;
+      const int n = (int)(t / args.tiles_m) * kBM + row;
+      const int m0 = (int)(t % args.tiles_m) * BN;
+      const int b = seg & 1;
+      const int cols = min(BN, args.M - m0);  // valid token columns of this tile
+      const bool owner = kb == 0;
       const bool n_ok = n < args.N;
-      const float swn = (n_ok && args.ws == nullptr) ? args.sw[n] : 0.f;
-      const float bn = (n_ok && args.bias != nullptr) ? __half2float(args.bias[n]) : 0.f;
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        if (m0 + c0 >= args.M) break;
-        float v[16];
-        if (nk > 0) {
-          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-        } else {
+      float swn = 0.f, bn = 0.f;
+      if (owner) {
+        // scales are inputs: fetch them while the tile is still accumulating
+        for (int j = et; j < cols; j += 128) s_sx[b * BN + j] = args.sx[m0 + j];
+        swn = n_ok ? args.sw[n] : 0.f;
+        bn = (n_ok && args.bias != nullptr) ? __half2float(args.bias[n]) : 0.f;
+      }
+      if (!mbar_wait(&acc_full[b], ((uint32_t)seg >> 1) & 1u)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t acc = tmem + (uint32_t)(b * C::kAccCols) + ((uint32_t)(q * 32) << 16);
+
+      if (!owner) {
+        // partial segment: hand the fp32 tile to the owner (column-major: coalesced per warp)
+        for (int c0 = 0; c0 < cols; c0 += 16) {
+          float v[16];
+          tmem_ld16(acc + (uint32_t)c0, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0.f;
+          for (int j = 0; j < 16; ++j) my_ws[(int64_t)(c0 + j) * kBM + row] = v[j];
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&acc_empty[b]);
+        epi_sync();  // all partial stores precede the release below (release is cumulative)
+        if (et == 0) st_release(&args.flags[cta], 1);
+        continue;
+      }
+
+      // owner: contributors are the CTAs whose ranges begin inside this tile
+      const int64_t tile_end = (t + 1) * (int64_t)KT;
+      int c_first = cta + 1, c_last = cta;
+      if (ke < KT) {
+        while (c_last + 1 < args.G && unit_begin(c_last + 1, args.U, args.G) < tile_end) ++c_last;
+        if (et == 0) {
+          for (int c = c_first; c <= c_last; ++c) {
+            uint32_t spins = 0;
+            while (ld_acquire(&args.flags[c]) == 0) {
+              if (++spins > (1u << 26)) {
+                set_device_status(kStatusMbarTimeout);
+                break;
+              }
+              __nanosleep(64);
+            }
+          }
+        }
+      }
+      epi_sync();  // s_sx filled; contributors' partials visible
+      for (int c0 = 0; c0 < cols; c0 += 16) {
+        float v[16];
+        tmem_ld16(acc + (uint32_t)c0, v);
+        for (int c = c_first; c <= c_last; c += 4) {
+          // up to four contributors' loads in flight before any add
+          float w4[4][16];
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            if (c + d <= c_last) {
+              const float* w = args.ws + (int64_t)(c + d) * BN * kBM + (int64_t)c0 * kBM + row;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) w4[d][j] = w[(int64_t)j * kBM];
+            }
+          }
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            if (c + d <= c_last) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] += w4[d][j];
+            }
+          }
         }
         if (!n_ok) continue;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int m = m0 + c0 + j;
-          if (m < args.M) {
-            if (args.ws != nullptr) {
-              args.ws[((int64_t)split * args.M + m) * args.N + n] = v[j];
-            } else {
-              __half r = __float2half_rn(v[j] * args.sx[m] * swn);
-              if (args.bias != nullptr) r = __float2half_rn(__half2float(r) + bn);
-              args.y[(int64_t)m * args.N + n] = r;
-            }
+          if (c0 + j < cols) {
+            const int m = m0 + c0 + j;
+            __half r = __float2half_rn(v[j] * s_sx[b * BN + c0 + j] * swn);
+            if (args.bias != nullptr) r = __float2half_rn(__half2float(r) + bn);
+            args.y[(int64_t)m * args.N + n] = r;
           }
         }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&acc_empty[b]);
+      if (c_last >= c_first) {
+        epi_sync();  // every thread has read the partials
+        if (et == 0)
+          for (int c = c_first; c <= c_last; ++c) args.flags[c] = 0;
       }
     }
   }
@@ -228,32 +387,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
-  }
-}
-
-// Sum split partials and apply the dequant epilogue. 4 outputs per thread.
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N,
-                                     const float* __restrict__ sx, const float* __restrict__ sw,
-                                     const __half* __restrict__ bias, __half* __restrict__ y) {
-  const int64_t total = (int64_t)M * N;
-  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < total;
-       i += (int64_t)gridDim.x * blockDim.x * 4) {
-    float4 acc = *reinterpret_cast<const float4*>(ws + i);
-    for (int s = 1; s < splits; ++s) {
-      float4 p = *reinterpret_cast<const float4*>(ws + (int64_t)s * total + i);
-      acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
-    }
-    const int m = (int)(i / N);
-    const int n = (int)(i % N);
-    const float a[4] = {acc.x, acc.y, acc.z, acc.w};
-    __half r[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      r[j] = __float2half_rn(a[j] * sx[m] * sw[n + j]);
-      if (bias != nullptr) r[j] = __float2half_rn(__half2float(r[j]) + __half2float(bias[n + j]));
-    }
-    *reinterpret_cast<__half2*>(y + i) = __halves2half2(r[0], r[1]);
-    *reinterpret_cast<__half2*>(y + i + 2) = __halves2half2(r[2], r[3]);
   }
 }
 
@@ -337,8 +470,7 @@ bool make_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int
 }
 
 template <int BN>
-cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& args, dim3 grid,
-                      cudaStream_t stream) {
+cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& args, cudaStream_t stream) {
   using C = Cfg<BN>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -347,89 +479,125 @@ cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const GemmAr
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  fp8_gemm_kernel<BN><<<grid, kThreads, C::kSmemBytes, stream>>>(mw, mx, args);
+  // Cooperative launch: every CTA is resident at once, which the stream-K
+  // fixup (owners wait for later CTAs' partials) relies on.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(args.G);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<BN>, mw, mx, args);
   MS_COUNT_LAUNCH();
-  return cudaGetLastError();
+  return e;
 }
 
-int choose_bn(int M) {
-  if (M <= 32) return 32;
-  if (M <= 64) return 64;
-  if (M <= 128) return 128;
-  return 256;
+constexpr size_t kFlagBytes = 1024;  // per-CTA partial-ready flags at the start of the workspace
+constexpr int kMinUnitsPerCta = 4;
+
+struct Plan {
+  int bn, ctas, dp;
+};
+
+// Token-tile width and scheduling for an M x N x K problem:
+//  * M <= 64 (small decode batches): one token tile; the few weight tiles are
+//    split along K by stream-K so every SM streams weights (partials are small);
+//  * 64 < M <= 256 (decode batches): whole tiles, no K split; the token tile
+//    width (64/96/128/256) is the one whose tile count fills the SMs best;
+//  * M > 256 (prefill): 256-token tiles, stream-K across the SMs.
+Plan make_plan(int M, int N, int K, int num_sms) {
+  const int64_t tiles_n = (N + kBM - 1) / kBM;
+  const int64_t KT = (K + kBK - 1) / kBK;
+  Plan p{256, 1, 0};
+  if (M > 64 && M <= 256) {
+    const int cands[4] = {256, 128, 96, 64};
+    double best = -1.0;
+    for (int bn : cands) {
+      const int64_t T = tiles_n * ((M + bn - 1) / bn);
+      const int64_t waves = (T + num_sms - 1) / num_sms;
+      const double eff = (double)T / ((double)waves * num_sms);
+      if (eff > best + 1e-9) {
+        best = eff;
+        p.bn = bn;
+      }
+    }
+    if (best >= 0.85) {
+      const int64_t T = tiles_n * ((M + p.bn - 1) / p.bn);
+      p.dp = 1;
+      p.ctas = (int)(T < num_sms ? T : num_sms);
+      return p;
+    }
+    p.bn = M <= 128 ? 128 : 256;
+  } else if (M <= 64) {
+    p.bn = M <= 32 ? 32 : 64;
+  }
+  const int64_t U = tiles_n * ((M + p.bn - 1) / p.bn) * KT;
+  int64_t g = U / kMinUnitsPerCta;
+  if (g < 1) g = 1;
+  if (g > num_sms) g = num_sms;
+  if (g > (int64_t)(kFlagBytes / sizeof(int))) g = kFlagBytes / sizeof(int);
+  p.ctas = (int)g;
+  return p;
 }
 
 }  // namespace
 
-void gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* splits_out) {
-  const int bn = choose_bn(M);
-  const int tiles = ((N + kBM - 1) / kBM) * ((M + bn - 1) / bn);
-  const int k_tiles = (K + kBK - 1) / kBK;
-  int splits = 1;
-  if (tiles * 2 <= num_sms) {
-    splits = num_sms / tiles;
-    const int max_splits = k_tiles / 4 > 0 ? k_tiles / 4 : 1;  // >= 4 K steps per split
-    if (splits > max_splits) splits = max_splits;
-    if (splits < 1) splits = 1;
-    // balance: equal K steps per split
-    const int per = (k_tiles + splits - 1) / splits;
-    splits = (k_tiles + per - 1) / per;
-  }
-  *bn_out = bn;
-  *splits_out = splits;
+void gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* ctas_out) {
+  const Plan p = make_plan(M, N, K, num_sms);
+  *bn_out = p.bn;
+  *ctas_out = p.ctas;
 }
 
 size_t gemm_workspace_bytes(int M, int N, int K, int num_sms) {
-  int bn, splits;
-  if (K % 16 != 0) return 0;
-  gemm_plan(M, N, K, num_sms, &bn, &splits);
-  return splits > 1 ? (size_t)splits * M * N * sizeof(float) : 0;
+  if (K % 16 != 0 || M <= 0) return 0;
+  const Plan p = make_plan(M, N, K, num_sms);
+  return p.dp ? 0 : kFlagBytes + (size_t)p.ctas * p.bn * kBM * sizeof(float);
 }
 
 cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,
                             void* y, int M, int N, int K, void* workspace, size_t workspace_bytes, int num_sms,
                             cudaStream_t stream) {
   if (M == 0 || N == 0) return cudaSuccess;
-  if (K % 16 != 0 || N % 4 != 0) {
+  if (K % 16 != 0) {
     dim3 grid((N + 127) / 128, M);
     fp8_gemm_simt_kernel<<<grid, 128, 0, stream>>>((const uint8_t*)xq, (const uint8_t*)wq, M, N, K, sx, sw,
                                                     (const __half*)bias, (__half*)y);
     MS_COUNT_LAUNCH();
     return cudaGetLastError();
   }
-  int bn, splits;
-  gemm_plan(M, N, K, num_sms, &bn, &splits);
-  const size_t need = splits > 1 ? (size_t)splits * M * N * sizeof(float) : 0;
-  if (need > workspace_bytes) return cudaErrorInvalidValue;
+  const Plan p = make_plan(M, N, K, num_sms);
+  const int bn = p.bn;
+  if (!p.dp && (gemm_workspace_bytes(M, N, K, num_sms) > workspace_bytes || workspace == nullptr))
+    return cudaErrorInvalidValue;
   CUtensorMap mw, mx;
   if (!make_map(&mw, wq, N, K, kBM) || !make_map(&mx, xq, M, K, bn)) return cudaErrorInvalidValue;
   GemmArgs args;
   args.M = M;
   args.N = N;
   args.K = K;
-  args.k_tiles = (K + kBK - 1) / kBK;
-  args.k_tiles_per_split = (args.k_tiles + splits - 1) / splits;
+  args.KT = (K + kBK - 1) / kBK;
+  args.tiles_m = (M + bn - 1) / bn;
+  args.T = (int64_t)((N + kBM - 1) / kBM) * args.tiles_m;
+  args.U = args.T * args.KT;
+  args.G = p.ctas;
+  args.dp = p.dp;
   args.sx = sx;
   args.sw = sw;
   args.bias = (const __half*)bias;
   args.y = (__half*)y;
-  args.ws = splits > 1 ? (float*)workspace : nullptr;
-  dim3 grid((N + kBM - 1) / kBM, (M + bn - 1) / bn, splits);
-  cudaError_t e;
+  args.flags = p.dp ? nullptr : (int*)workspace;
+  args.ws = p.dp ? nullptr : (float*)((char*)workspace + kFlagBytes);
   switch (bn) {
-    case 32: e = launch_tc<32>(mw, mx, args, grid, stream); break;
-    case 64: e = launch_tc<64>(mw, mx, args, grid, stream); break;
-    case 128: e = launch_tc<128>(mw, mx, args, grid, stream); break;
-    default: e = launch_tc<256>(mw, mx, args, grid, stream); break;
+    case 32: return launch_tc<32>(mw, mx, args, stream);
+    case 64: return launch_tc<64>(mw, mx, args, stream);
+    case 96: return launch_tc<96>(mw, mx, args, stream);
+    case 128: return launch_tc<128>(mw, mx, args, stream);
+    default: return launch_tc<256>(mw, mx, args, stream);
   }
-  if (e != cudaSuccess || splits == 1) return e;
-  const int64_t total = (int64_t)M * N;
-  int blocks = (int)((total / 4 + 255) / 256);
-  if (blocks > num_sms * 8) blocks = num_sms * 8;
-  splitk_reduce_kernel<<<blocks, 256, 0, stream>>>((const float*)workspace, splits, M, N, sx, sw,
-                                                    (const __half*)bias, (__half*)y);
-  MS_COUNT_LAUNCH();
-  return cudaGetLastError();
 }
 
 }  // namespace ms

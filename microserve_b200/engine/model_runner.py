@@ -351,14 +351,15 @@ class ModelRunner:
         from microserve_b200 import _lib
         lib = _lib.load()
         hf = self.hf_config
-        need = 0
+        gemm = decode = 0
         for bs in self.graph_bs:
             for m in self.model.modules():
                 if hasattr(m, "weight_fp8"):
-                    need = max(need, lib.ms_fp8_gemm_workspace_size(bs, m.out_features, m.in_features))
-            need = max(need, kernels.decode_workspace_bytes(bs, hf.num_attention_heads // tp.tp_size(),
-                                                            self.num_kv_heads, max_blocks, self.block_size))
-        kernels.workspace.reserve(need, self.device)
+                    gemm = max(gemm, lib.ms_fp8_gemm_workspace_size(bs, m.out_features, m.in_features))
+            decode = max(decode, kernels.decode_workspace_bytes(bs, hf.num_attention_heads // tp.tp_size(),
+                                                                self.num_kv_heads, max_blocks, self.block_size))
+        kernels.workspace.reserve(gemm, self.device, "gemm")
+        kernels.workspace.reserve(decode, self.device, "decode")
 
     @torch.inference_mode()
     def _warmup(self) -> None:

@@ -22,34 +22,37 @@ def _cuda(t: torch.Tensor, name: str) -> None:
 
 
 class _Workspace(threading.local):
-    """Per-thread, per-device scratch buffer for kernels that need one.
+    """Per-thread, per-device scratch buffers for kernels that need one, one
+    buffer per kernel family ("gemm", "decode").
 
-    Grows on demand outside CUDA-graph capture; inside a capture the buffer
-    must already be large enough (reserve() it before capturing)."""
+    The GEMM buffer starts zeroed: its first bytes hold tile flags that every
+    GEMM call leaves at zero again. Buffers grow on demand outside CUDA-graph
+    capture; inside a capture they must already be large enough (reserve()
+    before capturing)."""
 
     def __init__(self):
-        self.buf: dict[int, torch.Tensor] = {}
+        self.buf: dict[tuple[int, str], torch.Tensor] = {}
         # Buffers replaced by a larger one stay alive: captured CUDA graphs may
         # still hold their addresses.
         self.retired: list[torch.Tensor] = []
 
-    def get(self, nbytes: int, device: torch.device) -> torch.Tensor | None:
+    def get(self, nbytes: int, device: torch.device, name: str = "decode") -> torch.Tensor | None:
         if nbytes == 0:
             return None
         idx = device.index if device.index is not None else torch.cuda.current_device()
-        cur = self.buf.get(idx)
+        cur = self.buf.get((idx, name))
         if cur is None or cur.numel() < nbytes:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError(
-                    f"workspace of {nbytes} bytes needed during CUDA-graph capture; reserve it first")
+                    f"{name} workspace of {nbytes} bytes needed during CUDA-graph capture; reserve it first")
             if cur is not None:
                 self.retired.append(cur)
-            cur = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-            self.buf[idx] = cur
+            cur = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            self.buf[(idx, name)] = cur
         return cur
 
-    def reserve(self, nbytes: int, device: torch.device) -> None:
-        self.get(nbytes, device)
+    def reserve(self, nbytes: int, device: torch.device, name: str = "decode") -> None:
+        self.get(nbytes, device, name)
 
 
 workspace = _Workspace()
@@ -84,7 +87,7 @@ def fp8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Ten
     y = out if out is not None else torch.empty((M, N), dtype=torch.float16, device=xq.device)
     lib = _lib.load()
     nbytes = lib.ms_fp8_gemm_workspace_size(M, N, K)
-    ws = workspace.get(nbytes, xq.device)
+    ws = workspace.get(nbytes, xq.device, "gemm")
     check(lib.ms_fp8_gemm(ptr(xq), ptr(sx), ptr(wq), ptr(sw), ptr(bias), ptr(y), M, N, K, ptr(ws),
                           0 if ws is None else ws.numel(), stream_ptr()), "ms_fp8_gemm")
     return y
