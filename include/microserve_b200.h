@@ -118,6 +118,21 @@ int ms_paged_decode_fp8(const void* q, const void* k_cache, const void* v_cache,
                         int Hq, int Hkv, int head_dim, int block_size, int max_blocks, float softmax_scale,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ms_paged_decode_fp8 without a workspace argument and without any allocation.
+ * No counterpart in the reference: it exists for callers that cannot allocate
+ * device memory where attention runs (inside another framework's memory pool,
+ * embedders that forbid cudaMalloc after start-up, callers holding only a
+ * stream). The context-split partials go to a 4 MiB buffer built into the
+ * library, which every GPU that loads the library keeps until exit; batches
+ * needing more return MS_ERR_UNSUPPORTED (use ms_paged_decode_fp8). The first
+ * call on a device looks up the buffer's device address, so make it before
+ * any stream capture. All calls on a device share the buffer: calls that
+ * overlap on the GPU race and must be serialised by the caller. */
+int ms_paged_decode_fp8_noalloc(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
+                                const float* v_scale, const int32_t* seqlens, const int32_t* block_tables, void* out,
+                                int B, int Hq, int Hkv, int head_dim, int block_size, int max_blocks,
+                                float softmax_scale, void* stream);
+
 /* Causal chunked-prefill attention over the paged FP8 cache, any number of
  * sequences: sequence s has queries q[cu_q[s] .. cu_q[s+1]) at positions
  * kv_lens[s] - q_len_s .. kv_lens[s] - 1 and attends to its first kv_lens[s]

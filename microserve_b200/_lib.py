@@ -33,6 +33,7 @@ SIGNATURES: dict[str, tuple] = {
     "ms_qkv_post": (i32, [vp, i64, i32, i32, i32, vp, vp, f32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "ms_paged_decode_workspace_size": (sz, [i32, i32, i32, i32, i32]),
     "ms_paged_decode_fp8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32, vp, sz, vp]),
+    "ms_paged_decode_fp8_noalloc": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32, vp]),
     "ms_paged_prefill_fp8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i64, i32, i32, i32, i32, i32, f32, vp]),
     "ms_varlen_prefill": (i32, [vp, vp, vp, vp, vp, i32, i64, i32, i32, i32, f32, vp]),
 }

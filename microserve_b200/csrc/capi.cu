@@ -174,6 +174,37 @@ int ms_paged_decode_fp8(const void* q, const void* k_cache, const void* v_cache,
                     "ms_paged_decode_fp8");
 }
 
+int ms_paged_decode_fp8_noalloc(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
+                                const float* v_scale, const int32_t* seqlens, const int32_t* block_tables, void* out,
+                                int B, int Hq, int Hkv, int head_dim, int block_size, int max_blocks,
+                                float softmax_scale, void* stream) {
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || block_size <= 0 || max_blocks <= 0)
+    return fail(MS_ERR_INVALID, "ms_paged_decode_fp8_noalloc: bad sizes");
+  if (B == 0) return MS_OK;
+  if (!q || !k_cache || !v_cache || !k_scale || !v_scale || !seqlens || !block_tables || !out)
+    return fail(MS_ERR_INVALID, "ms_paged_decode_fp8_noalloc: null pointer");
+  if (head_dim != 128 || Hq % Hkv != 0 || Hq / Hkv > 8 || block_size % 16 != 0)
+    return fail(MS_ERR_UNSUPPORTED, "ms_paged_decode_fp8_noalloc: head_dim=%d Hq=%d Hkv=%d block_size=%d unsupported",
+                head_dim, Hq, Hkv, block_size);
+  const int splits = ms::decode_num_splits(B, Hkv, max_blocks, block_size, num_sms());
+  const size_t need = ms::decode_workspace_bytes(B, Hq, splits);
+  const size_t have = ms::decode_noalloc_scratch_bytes();
+  if (need > have)
+    return fail(MS_ERR_UNSUPPORTED,
+                "ms_paged_decode_fp8_noalloc: this batch needs %zu bytes of scratch but the built-in buffer holds "
+                "%zu bytes; use ms_paged_decode_fp8 with a caller-provided workspace",
+                need, have);
+  void* ws = nullptr;
+  if (need > 0) {
+    const cudaError_t e = ms::decode_noalloc_scratch(&ws);
+    if (e != cudaSuccess) return check_cuda(e, "ms_paged_decode_fp8_noalloc: scratch address");
+  }
+  return check_cuda(ms::launch_decode_attention(q, k_cache, v_cache, k_scale, v_scale, seqlens, block_tables, out, B,
+                                                Hq, Hkv, head_dim, block_size, max_blocks, softmax_scale, splits, ws,
+                                                S(stream)),
+                    "ms_paged_decode_fp8_noalloc");
+}
+
 int ms_paged_prefill_fp8(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
                          const float* v_scale, const int32_t* block_tables, const int32_t* cu_q,
                          const int32_t* kv_lens, void* out, int num_seqs, int64_t total_q, int Hq, int Hkv,

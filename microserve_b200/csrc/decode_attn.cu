@@ -27,6 +27,8 @@
 //    tiles and are merged through shared memory at the end. Long contexts with
 //    few sequences are split over CTAs (flash-decoding); partial (m, l, o)
 //    rows go to a workspace and a second kernel merges them.
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -374,6 +376,48 @@ cudaError_t launch_decode_attention(const void* q, const void* k_cache, const vo
     MS_COUNT_LAUNCH();
   }
   return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant (ms_paged_decode_fp8_noalloc).
+//
+// Some callers cannot allocate device memory at the point where they run
+// attention: code running inside another framework's allocator or memory
+// pool, embedders that forbid cudaMalloc after start-up, or callers whose
+// only handle is a stream. For them the context-split partials live in a
+// fixed buffer compiled into the library. Every GPU that loads the library
+// holds this buffer (kNoAllocScratchBytes) until the process exits. All calls
+// on a device share it: calls that overlap on the GPU (two streams, or two
+// host threads) race on it and must be serialised by the caller. Nothing in
+// it needs to start at zero: each call writes every partial it later reads.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+}  // namespace
+
+size_t decode_noalloc_scratch_bytes() { return kNoAllocScratchBytes; }
+
+// Device address of the built-in scratch on the current device. Host code
+// cannot use the symbol itself (it names a host-side stand-in), so the
+// address is looked up once per device, with that device current; the first
+// call on a device therefore must not happen during stream capture.
+cudaError_t decode_noalloc_scratch(void** ptr) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> g(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = p;
+  }
+  *ptr = addr[dev];
+  return cudaSuccess;
 }
 
 }  // namespace ms

@@ -22,6 +22,8 @@ cudaError_t launch_qkv_post(const void* qkv, int64_t T, int q_heads, int kv_head
 
 int decode_num_splits(int B, int Hkv, int max_blocks, int block_size, int num_sms);
 size_t decode_workspace_bytes(int B, int Hq, int splits);
+size_t decode_noalloc_scratch_bytes();
+cudaError_t decode_noalloc_scratch(void** ptr);
 cudaError_t launch_decode_attention(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
                                     const float* v_scale, const int32_t* seqlens, const int32_t* block_tables,
                                     void* out, int B, int Hq, int Hkv, int head_dim, int block_size, int max_blocks,
