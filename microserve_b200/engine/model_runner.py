@@ -296,16 +296,7 @@ class ModelRunner:
         logits = self.model.compute_logits(hidden)
         if tp.tp_size() == 1:
             return logits, logits.argmax(dim=-1)
-        # vocab-parallel greedy: reduce (max, first index) pairs over ranks
-        local_max, local_idx = logits.float().max(dim=-1)
-        local_idx = local_idx + self.model.lm_head.vocab_start
-        pair = torch.stack([local_max, local_idx.float()], dim=-1)
-        gathered = [torch.empty_like(pair) for _ in range(tp.tp_size())]
-        torch.distributed.all_gather(gathered, pair, group=tp.tp_group())
-        allp = torch.stack(gathered, dim=0)  # [t, B, 2]
-        best = allp[..., 0].argmax(dim=0)    # first rank with the max = smallest index on ties
-        idx = allp[..., 1].gather(0, best.unsqueeze(0)).squeeze(0).to(torch.int64)
-        return logits, idx
+        return logits, tp.tp_argmax(logits, self.model.lm_head.vocab_start)
 
     def _sample_rows(self, seqs: list[Sequence], hidden: torch.Tensor) -> list[int | None]:
         logits, greedy = self._logits_and_argmax(hidden)

@@ -52,3 +52,19 @@ def all_reduce_max_(x: torch.Tensor) -> torch.Tensor:
     if _SIZE > 1:
         dist.all_reduce(x, op=dist.ReduceOp.MAX, group=_GROUP)
     return x
+
+
+def tp_argmax(local_logits: torch.Tensor, vocab_start: int) -> torch.Tensor:
+    """Greedy token over a vocab-parallel logits slice [B, V_local]: the global
+    argmax with the smallest index winning ties (torch.argmax's rule), from an
+    all-gather of one (max, index) pair per row instead of the logits."""
+    local_max, local_idx = local_logits.float().max(dim=-1)
+    if _SIZE == 1:
+        return local_idx
+    local_idx = local_idx + vocab_start
+    pair = torch.stack([local_max, local_idx.to(torch.float64).float()], dim=-1)
+    gathered = [torch.empty_like(pair) for _ in range(_SIZE)]
+    dist.all_gather(gathered, pair, group=_GROUP)
+    allp = torch.stack(gathered, dim=0)  # [t, B, 2]; ranks hold ascending vocab ranges
+    best = allp[..., 0].argmax(dim=0)    # first (lowest) rank with the max value
+    return allp[..., 1].gather(0, best.unsqueeze(0)).squeeze(0).to(torch.int64)
