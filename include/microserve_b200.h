@@ -14,7 +14,9 @@
  * fp8 is e4m3 ("float8_e4m3fn"), scales are fp32.
  *
  * FP8 encoding (bit-exact with the reference):
- *   scale = max(amax, 1e-8) / 448;  code = e4m3_rn_satfinite(clamp(x / scale, -448, 448))
+ *   scale = max(amax, 1e-8) * fl32(1/448);  code = e4m3_rn_satfinite(clamp(x / scale, -448, 448))
+ *   (the reference writes `/ 448`; its Triton kernels and torch's CUDA division evaluate
+ *   that as a multiply by the fp32 reciprocal, which is what its GPU outputs show)
  *
  * Each declaration names the reference interface it replaces
  * (gssg1/microserve, path:line).

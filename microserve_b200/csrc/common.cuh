@@ -1,11 +1,15 @@
 // Shared device helpers for the microserve-b200 kernels (sm_100a only).
 //
 // Numerics contract: every FP8 encode in this library is
-//   scale = max(amax, 1e-8f) / 448.0f       (IEEE fp32 divide)
+//   scale = max(amax, 1e-8f) * fl32(1/448)
 //   q     = e4m3(clamp(x / scale, -448, 448)) (IEEE divide, round-to-nearest-even, satfinite)
-// which is the formula of the reference's Triton kernels
-// (microserve/layers/fp8_linear.py:20-21, microserve/layers/fp8_kv_cache.py:34-37).
-// The library is compiled without --use_fast_math so that `/` is div.rn.f32.
+// The reference writes `max(amax, 1e-8) / 448.0` (microserve/layers/fp8_linear.py:20-21,
+// :52; microserve/layers/fp8_kv_cache.py:34-37), but both of its executions of that
+// expression - the Triton kernels and torch on CUDA (a tensor divided by a scalar) -
+// multiply by the fp32 reciprocal, which differs from an IEEE divide by one ulp for about
+// half of the inputs; the golden outputs of the reference's own GPU kernels
+// (tests/golden/reference_gpu.pt) pin this. The library is compiled without
+// --use_fast_math so that `x / scale` is div.rn.f32.
 #pragma once
 
 #include <cuda.h>
@@ -47,7 +51,7 @@ __device__ __forceinline__ void set_device_status(int code) {
 // FP8 helpers
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float fp8_scale_from_amax(float amax) {
-  return fmaxf(amax, 1e-8f) / MS_FP8_MAX;
+  return fmaxf(amax, 1e-8f) * (1.0f / MS_FP8_MAX);
 }
 
 // Encode two fp32 values (already divided by the scale) into two e4m3 bytes,

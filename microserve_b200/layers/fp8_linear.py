@@ -1,7 +1,8 @@
 """Dynamic FP8 e4m3 W8A8 linear (the reference's microserve/layers/fp8_linear.py).
 
 FP8DynamicLinear(source) quantises the source weight once, per output channel
-(scale = max(amax_row, 1e-8) / 448, :49-56), and its forward quantises the
+(scale = max(amax_row, 1e-8) * fl32(1/448), :49-56: the reference writes
+`/ 448`, which torch evaluates on the GPU as a multiply by the fp32 reciprocal), and its forward quantises the
 activation rows dynamically (:14-23) and runs the tcgen05 FP8 GEMM with the
 per-row x per-channel dequant epilogue (:26-45). Weight quantisation runs on
 the GPU through the library's row quantiser (the same formula).
@@ -19,6 +20,7 @@ from microserve_b200.layers.linear import LinearBase
 from microserve_b200.utils import dist as tp
 
 FP8_MAX = 448.0  # largest finite value of torch.float8_e4m3fn
+INV_FP8_MAX = 1.0 / FP8_MAX  # applied in fp32, as torch applies `/ 448` on the GPU
 
 
 class FP8DynamicLinear(nn.Module):
@@ -29,13 +31,13 @@ class FP8DynamicLinear(nn.Module):
             raise ValueError("FP8DynamicLinear quantises on the GPU: move the model to CUDA first")
         w16 = w.to(torch.float16).contiguous()
         if source.full_row_amax is not None:
-            scales = source.full_row_amax.float().clamp_min(1e-8) / FP8_MAX
+            scales = source.full_row_amax.float().clamp_min(1e-8) * INV_FP8_MAX
             packed = (w16.float() / scales[:, None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
         elif w.dtype == torch.float16:
             packed, scales = kernels.quantize_rows_fp8(w16)
         else:  # fp32 master weights: the reference's formula on the original values
             wf = w.float()
-            scales = wf.abs().amax(dim=1).clamp_min(1e-8) / FP8_MAX
+            scales = wf.abs().amax(dim=1).clamp_min(1e-8) * INV_FP8_MAX
             packed = (wf / scales[:, None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
         self.register_buffer("weight_fp8", packed.contiguous())
         self.register_buffer("weight_scale", scales.contiguous())

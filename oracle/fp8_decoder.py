@@ -12,8 +12,8 @@ tests/test_fp8_kv_attention.py:30-36,63-70,96-105).
 
 Pinning: tests/golden/ holds vectors produced by running the reference
 itself - its CPU-runnable modules in this container (make_golden.py) and its
-Triton kernels on a B200 (make_golden_gpu.py) - and tests/test_oracle.py
-checks this module against them.
+Triton kernels on a B200 (make_golden_gpu.py) - and tests/test_oracle_cpu.py
+and tests/test_reference_golden.py check this module against them.
 """
 from __future__ import annotations
 
@@ -24,13 +24,22 @@ import torch.nn.functional as F
 
 FP8_MAX = 448.0
 E4M3 = torch.float8_e4m3fn
+# The reference writes `max(amax, 1e-8) / 448`, but both places that evaluate it on the GPU
+# (its Triton kernels and torch's CUDA tensor-by-scalar division) multiply by the fp32
+# reciprocal; tests/golden/reference_gpu.pt (the reference's own outputs) pins that.
+INV_FP8_MAX = torch.tensor(1.0 / FP8_MAX, dtype=torch.float32)
+
+
+def fp8_scale(amax: torch.Tensor) -> torch.Tensor:
+    """Per-row scale of the reference's FP8 encode (fp8_linear.py:20, :52; fp8_kv_cache.py:34-35)."""
+    return amax.float().clamp_min(1e-8) * INV_FP8_MAX
 
 
 # ---------------------------------------------------------------- FP8 linear
 def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-row dynamic quant (microserve/layers/fp8_linear.py:14-23)."""
     xf = x.float()
-    s = xf.abs().amax(dim=-1).clamp_min(1e-8) / FP8_MAX
+    s = fp8_scale(xf.abs().amax(dim=-1))
     q = (xf / s[..., None]).clamp(-FP8_MAX, FP8_MAX).to(E4M3)
     return q, s
 
@@ -38,7 +47,7 @@ def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 def quantize_weight(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Offline per-output-channel weight quant (microserve/layers/fp8_linear.py:51-54)."""
     wf = w.detach().float()
-    s = wf.abs().amax(dim=1).clamp_min(1e-8) / FP8_MAX
+    s = fp8_scale(wf.abs().amax(dim=1))
     q = (wf / s[:, None]).clamp(-FP8_MAX, FP8_MAX).to(E4M3)
     return q, s
 
@@ -100,11 +109,11 @@ def rope(positions, q, k, cos_cache, sin_cache):
 # ------------------------------------------------------------- FP8 KV cache
 def store_kv(k, v, k_cache, v_cache, k_scale, v_scale, slots) -> None:
     """store_fp8_kvcache (microserve/layers/fp8_kv_cache.py:24-39): per (token, head)
-    scale = max(amax_d, 1e-8)/448, codes = e4m3(clamp(x/scale)), scattered to slot."""
+    scale = max(amax_d, 1e-8)*fl32(1/448), codes = e4m3(clamp(x/scale)), scattered to slot."""
     bs = k_cache.shape[1]
     for src, cache, sc in ((k, k_cache, k_scale), (v, v_cache, v_scale)):
         xf = src.float()
-        s = xf.abs().amax(dim=-1).clamp_min(1e-8) / FP8_MAX
+        s = fp8_scale(xf.abs().amax(dim=-1))
         q = (xf / s[..., None]).clamp(-FP8_MAX, FP8_MAX).to(E4M3)
         blk, off = slots // bs, slots % bs
         cache[blk, off] = q

@@ -41,11 +41,17 @@ def test_oracle_silu_mul_matches_reference_module(layers):
 
 
 @pytest.mark.parametrize("name", ["w50x70", "w128x256"])
-def test_oracle_weight_quant_matches_reference_module(layers, name):
+def test_oracle_weight_quant_vs_reference_module_on_cpu(layers, name):
+    """The reference module evaluated on the CPU divides by 448 exactly; on the GPU (where
+    the reference quantises) it multiplies by the fp32 reciprocal, which the oracle follows
+    (pinned bit-exactly by tests/test_reference_golden.py). The two agree to one ulp in the
+    scale and in all but a handful of codes."""
     g = layers["weight_quant_" + name]
     q, s = O.quantize_weight(g["weight"].float())
-    assert torch.equal(s, g["scales"])
-    assert torch.equal(q.view(torch.uint8), g["codes"])
+    assert torch.allclose(s, g["scales"], rtol=2.5e-7, atol=0)
+    assert (q.view(torch.uint8) != g["codes"]).float().mean().item() < 1e-3
+    exact = g["weight"].float().abs().amax(1).clamp_min(1e-8) / 448.0  # the CPU evaluation
+    assert torch.equal(exact, g["scales"])
     assert g["scales"][3].item() == pytest.approx(1e-8 / 448)  # the all-zero channel
 
 
