@@ -155,13 +155,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 
-// Wait until the barrier's phase `phase` completed. Gives up after ~`limit`
-// polls (each try_wait already suspends for a hardware-defined interval),
-// records kStatusMbarTimeout and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t limit = (1u << 24)) {
-  for (uint32_t i = 0; i < limit; ++i) {
+// Nanoseconds of the GPU's global timer.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Upper bound of any in-kernel wait. Legitimate waits last microseconds to
+// milliseconds; this only ends a wait whose event can no longer come.
+constexpr uint64_t kWaitLimitNs = 4000000000ull;
+
+// Wait until the barrier's phase `phase` completed. try_wait already suspends
+// the thread in hardware until the phase completes (or a short time limit
+// passes), so the loop adds no sleep of its own: a __nanosleep here delays the
+// wake-up by its own granularity. Gives up after kWaitLimitNs, records
+// kStatusMbarTimeout and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, phase)) return true;
-    if (i > 64) __nanosleep(32);
+    if ((i & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) break;
   }
   set_device_status(kStatusMbarTimeout);
   return false;

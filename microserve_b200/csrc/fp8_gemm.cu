@@ -14,13 +14,17 @@
 // tile shape over more token tiles.
 //
 // Per CTA: warp 0 issues TMA loads (128B-swizzled, K-major) into a ring of
-// shared-memory stages; warp 1 owns the TMEM accumulator and issues
-// tcgen05.mma (kind::f8f6f4, 128 x BN x 32 per instruction, 4 per 128-byte K
-// step); warps 2-5 drain TMEM with tcgen05.ld and apply the dequant epilogue.
-// The kernel is persistent and stream-K scheduled: the tiles x K-steps work is
-// split evenly over at most one CTA per SM, and tiles shared by two CTAs are
-// summed in-kernel (fp32 partials in the caller's workspace), so there is no
-// wave quantisation and no separate reduction pass.
+// shared-memory stages of CH 128-byte K chunks each (one TMA box per operand
+// per stage); warp 1 owns the TMEM accumulator and issues tcgen05.mma
+// (kind::f8f6f4, 128 x BN x 32 per instruction, 4 per chunk); warps 2-5 drain
+// TMEM with tcgen05.ld and apply the dequant epilogue. The kernel is
+// persistent: whole tiles round-robin when they fill the SMs evenly, else
+// stream-K (the tiles x K-steps work split evenly over at most one CTA per SM,
+// tiles shared by two CTAs summed in-kernel from fp32 partials in the caller's
+// workspace), so there is no wave quantisation and no separate reduction pass.
+// Programmatic dependent launch: the weight loads of the first stage and the
+// CTA prologue may overlap the preceding grid; everything that reads its
+// results (activations, token scales, workspace, output) waits for it.
 //
 // Every wait is bounded (common.cuh: mbar_wait); on a timeout the kernel
 // records a device status, skips the rest and still frees its TMEM.
@@ -33,17 +37,17 @@
 namespace ms {
 namespace {
 
-constexpr int kBM = 128;       // weight rows per tile (MMA M)
-constexpr int kBK = 128;       // K bytes per stage (one 128B swizzle span)
-constexpr int kThreads = 192;  // 6 warps
+constexpr int kBM = 128;          // weight rows per tile (MMA M)
+constexpr int kChunk = 128;       // K bytes per swizzle span (one 128B-swizzled tile row)
+constexpr int kThreads = 192;     // 6 warps
 
 struct GemmArgs {
   int M, N, K;
-  int KT;       // K tiles of kBK bytes
+  int KT;       // K steps of CH chunks
   int tiles_m;  // token tiles
   int64_t T;    // output tiles
   int64_t U;    // work units = tiles * KT
-  int G;        // CTAs (persistent, all co-resident)
+  int G;        // CTAs (persistent, one per SM at most)
   int dp;       // 1: whole tiles round-robin (no K split); 0: stream-K
   const float* sx;
   const float* sw;
@@ -53,18 +57,27 @@ struct GemmArgs {
   int* flags;  // [G] partial-ready flags; zero before and after every launch
 };
 
-template <int BN>
+// BN: token columns per tile (MMA N). CH: 128-byte K chunks per pipeline stage.
+// With CH = 2 the operands are described by 3D tensor maps (chunk, row, byte)
+// so ONE TMA box brings two chunks (e.g. 32 KB of weights): TMA throughput per
+// SM is bounded by boxes per second, not bytes, for boxes up to 32 KB.
+template <int BN, int CH>
 struct Cfg {
-  static constexpr int kABytes = kBM * kBK;
-  static constexpr int kBBytes = BN * kBK;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : (BN >= 96 ? 7 : 8));
+  static constexpr int kChunkA = kBM * kChunk;  // one K chunk of the weight tile (16 KB)
+  static constexpr int kChunkB = BN * kChunk;   // one K chunk of the token tile
+  static constexpr int kABytes = CH * kChunkA;
+  static constexpr int kStageBytes = CH * (kChunkA + kChunkB);
   static constexpr int kAccCols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));  // TMEM columns
   static constexpr int kTmemCols = 2 * kAccCols;  // two accumulators (double buffer)
-  static constexpr int kSxBytes = 2 * BN * 4;  // token scales of the current tile, double-buffered
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kSxBytes;
+  static constexpr int kSxBytes = 2 * BN * 4;     // token scales of the current tile, double-buffered
+  static constexpr int kBarBytes = 256;
+  static constexpr int kFit = (227 * 1024 - 1024 - kBarBytes - kSxBytes) / kStageBytes;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + kBarBytes + kSxBytes;
   // tcgen05 instruction descriptor: D=f32, A=B=e4m3, both K-major, N=BN, M=128.
   static constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+  static_assert(kStages >= 2, "shared memory budget");
+  static_assert(BN % 16 == 0 && BN <= 256, "MMA N");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -86,6 +99,25 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint32_t dst
           dst),
       "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// One stage of an operand: CH chunks starting at K step k, rows from `row`.
+template <int CH>
+__device__ __forceinline__ void load_stage(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int k, int row) {
+  if constexpr (CH == 1) {
+    tma_load_2d(map, dst, bar, k * kChunk, row);
+  } else {
+    tma_load_3d(map, dst, bar, 0, row, k * CH);
+  }
 }
 
 __device__ __forceinline__ void umma_f8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accum) {
@@ -163,21 +195,34 @@ __device__ __forceinline__ int k_rotation(const GemmArgs& a, int64_t t, int kb, 
   return (int)(((t / a.tiles_m) * 5) % (ke - kb));
 }
 
-// Stream-K persistent GEMM. The U = tiles * KT work units (one 128-byte K
-// step of one 128 x BN output tile) are split evenly over G co-resident CTAs;
-// each CTA walks its contiguous range tile by tile ("segments"). A segment
-// that starts at k = 0 owns its tile: when the tile continues in later CTAs,
-// the owner adds their fp32 partials (ws, flagged ready) before the epilogue.
-// A segment that starts mid-tile stores its partial and raises its flag.
-// The accumulator is double-buffered in TMEM so a tile's epilogue overlaps
-// the next tile's main loop.
-template <int BN>
+// Programmatic dependent launch: wait for the preceding grid's results / let the
+// next grid start its prologue. Both are no-ops when the launch did not opt in.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Persistent GEMM, data-parallel or stream-K. In stream-K mode the U = tiles *
+// KT work units (one K step of one 128 x BN output tile) are split evenly over
+// G CTAs; each CTA walks its contiguous range tile by tile ("segments"). A
+// segment that starts at k = 0 owns its tile: when the tile continues in later
+// CTAs, the owner adds their fp32 partials (ws, flagged ready) before the
+// epilogue. A segment that starts mid-tile stores its partial and raises its
+// flag. The accumulator is double-buffered in TMEM so a tile's epilogue
+// overlaps the next tile's main loop.
+//
+// Roles: warp 0 lane 0 issues TMA, warp 1 owns TMEM and lane 0 issues MMAs,
+// warps 2-5 are the epilogue (TMEM lane quarter = warp % 4). The other lanes
+// of warps 0-1 wait at __syncwarp so every warp reaches the final block
+// barrier converged (a partially arrived warp would count as arrived).
+template <int BN, int CH>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     GemmArgs args) {
-  using C = Cfg<BN>;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // 1024-byte alignment required by the 128B swizzle atoms.
+  using C = Cfg<BN, CH>;
+  // The 128B swizzle atoms need 1024-byte alignment. The dynamic window is only
+  // guaranteed 16-byte aligned (it follows any static shared memory), so align by
+  // hand; declaring the array __align__(1024) would let the compiler fold the
+  // adjustment below to zero.
+  extern __shared__ __align__(16) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
@@ -185,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + C::kStages;  // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  float* s_sx = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes + 256);  // [2][BN]
+  float* s_sx = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes + C::kBarBytes);  // [2][BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
@@ -221,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       SegIter it(args, cta);
       int64_t t;
       int kb, ke;
-      bool ok = true;
+      bool ok = true, waited = false;
       while (ok && it.next(t, kb, ke)) {
         const int n0 = (int)(t / args.tiles_m) * kBM;
         const int m0 = (int)(t % args.tiles_m) * BN;
@@ -236,11 +281,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int k = kb + (j + rot) % nk;
           unsigned char* sa = smem + s * C::kStageBytes;
           mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-          tma_load_2d(&tmap_w, smem_u32(sa), &full[s], k * kBK, n0);
-          tma_load_2d(&tmap_x, smem_u32(sa + C::kABytes), &full[s], k * kBK, m0);
+          // weights never depend on the preceding grid: stream them before waiting for it
+          load_stage<CH>(&tmap_w, smem_u32(sa), &full[s], k, n0);
+          if (!waited) {
+            pdl_wait();
+            waited = true;
+          }
+          load_stage<CH>(&tmap_x, smem_u32(sa + C::kABytes), &full[s], k, m0);
         }
       }
+      pdl_trigger();  // every load of this CTA is issued
     }
+    __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
@@ -265,9 +317,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = smem_u32(smem + s * C::kStageBytes);
           const uint32_t b_addr = a_addr + C::kABytes;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 32; ++kk) {
-            umma_f8(acc, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), C::kIdesc,
-                    (j > 0 || kk > 0) ? 1u : 0u);
+          for (int c = 0; c < CH; ++c) {
+#pragma unroll
+            for (int kk = 0; kk < kChunk / 32; ++kk) {
+              umma_f8(acc, smem_desc_sw128(a_addr + c * C::kChunkA + kk * 32),
+                      smem_desc_sw128(b_addr + c * C::kChunkB + kk * 32), C::kIdesc,
+                      (j > 0 || c > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           umma_commit(&empty[s]);
         }
@@ -276,12 +332,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++seg;
       }
     }
+    __syncwarp();
   } else {
     // ---------------- epilogue (warps 2..5 -> TMEM lane quarters 2,3,0,1) ----------------
     const int q = warp & 3;
     const int row = q * 32 + lane;  // row within the 128-row weight tile
     const int et = threadIdx.x - 64;
     float* my_ws = args.ws + (int64_t)cta * BN * kBM;
+    __half* __restrict__ y = args.y;
+    const int64_t N = args.N;
+    pdl_wait();  // token scales come from the preceding grid; the workspace may be in use until it ends
     int seg = -1;
     SegIter it(args, cta);
     int64_t t;
@@ -326,14 +386,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ke < KT) {
         while (c_last + 1 < args.G && unit_begin(c_last + 1, args.U, args.G) < tile_end) ++c_last;
         if (et == 0) {
+          const uint64_t t0 = global_ns();
           for (int c = c_first; c <= c_last; ++c) {
             uint32_t spins = 0;
             while (ld_acquire(&args.flags[c]) == 0) {
-              if (++spins > (1u << 26)) {
+              if ((++spins & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) {
                 set_device_status(kStatusMbarTimeout);
                 break;
               }
-              __nanosleep(64);
             }
           }
         }
@@ -362,14 +422,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!n_ok) continue;
+        // all 16 results in registers first, then the stores back to back
+        const float4* sxv = reinterpret_cast<const float4*>(s_sx + b * BN + c0);
+        float sc[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (c0 + j < cols) {
-            const int m = m0 + c0 + j;
-            __half r = __float2half_rn(v[j] * s_sx[b * BN + c0 + j] * swn);
-            if (args.bias != nullptr) r = __float2half_rn(__half2float(r) + bn);
-            args.y[(int64_t)m * args.N + n] = r;
-          }
+        for (int g = 0; g < 4; ++g) {
+          const float4 f = sxv[g];
+          sc[4 * g] = f.x;
+          sc[4 * g + 1] = f.y;
+          sc[4 * g + 2] = f.z;
+          sc[4 * g + 3] = f.w;
+        }
+        __half r[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(v[j] * sc[j] * swn);
+        if (args.bias != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(__half2float(r[j]) + bn);
+        }
+        __half* yp = y + (int64_t)(m0 + c0) * N + n;
+        if (c0 + 16 <= cols) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) yp[j * N] = r[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c0 + j < cols) yp[j * N] = r[j];
         }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -428,23 +506,29 @@ EncodeTiledFn get_encode_fn() {
 struct MapKey {
   const void* ptr;
   int64_t rows, cols;
-  int box_rows;
+  int box_rows, ch;
   bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows;
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows && ch == o.ch;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     return std::hash<const void*>()(k.ptr) ^ (std::hash<int64_t>()(k.rows) * 31) ^
-           (std::hash<int64_t>()(k.cols) * 131) ^ (size_t)k.box_rows * 7;
+           (std::hash<int64_t>()(k.cols) * 131) ^ (size_t)k.box_rows * 7 ^ (size_t)k.ch * 1009;
   }
 };
 
-// 2D K-major e4m3 matrix [rows, cols] (cols contiguous), box = [box_rows, 128 bytes], 128B swizzle.
-bool make_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+// K-major e4m3 matrix [rows, cols] (cols contiguous), 128-byte swizzle.
+//  ch == 1: 2D map (byte, row), box = [box_rows, 128 bytes]; cols need only be a
+//           multiple of 16 (out-of-range K reads as zero).
+//  ch == 2: 3D map (byte within a 128-byte chunk, row, chunk) with strides
+//           (cols, 128), box = [2 chunks][box_rows][128 bytes]: one box is two
+//           consecutive K-chunk tiles, each laid out exactly as a 2D box. Needs
+//           cols % 128 == 0 (a chunk past K reads as zero).
+bool make_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int box_rows, int ch) {
   static std::mutex mu;
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-  MapKey key{ptr, rows, cols, box_rows};
+  MapKey key{ptr, rows, cols, box_rows, ch};
   {
     std::lock_guard<std::mutex> g(mu);
     auto it = cache.find(key);
@@ -455,13 +539,25 @@ bool make_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int
   }
   EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (ch == 1) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols};
+    cuuint32_t box[2] = {(cuuint32_t)kChunk, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    if (cols % kChunk != 0) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)kChunk, (cuuint64_t)rows, (cuuint64_t)(cols / kChunk)};
+    cuuint64_t strides[2] = {(cuuint64_t)cols, (cuuint64_t)kChunk};
+    cuuint32_t box[3] = {(cuuint32_t)kChunk, (cuuint32_t)box_rows, (cuuint32_t)ch};
+    cuuint32_t estr[3] = {1, 1, 1};
+    r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) return false;
   std::lock_guard<std::mutex> g(mu);
   if (cache.size() > 4096) cache.clear();
@@ -469,18 +565,18 @@ bool make_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int
   return true;
 }
 
-template <int BN>
+template <int BN, int CH>
 cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& args, cudaStream_t stream) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, CH>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<BN, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  // Cooperative launch: every CTA is resident at once, which the stream-K
-  // fixup (owners wait for later CTAs' partials) relies on.
+  // Stream-K owners wait for later CTAs' partials, so every CTA must be
+  // resident at once: a cooperative launch of at most one CTA per SM.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(args.G);
   cfg.blockDim = dim3(kThreads);
@@ -490,53 +586,57 @@ cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const GemmAr
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<BN>, mw, mx, args);
+  cfg.numAttrs = args.dp ? 0 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<BN, CH>, mw, mx, args);
   MS_COUNT_LAUNCH();
   return e;
+}
+
+template <int BN>
+cudaError_t launch_bn(int ch, const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& args,
+                      cudaStream_t stream) {
+  return ch == 2 ? launch_tc<BN, 2>(mw, mx, args, stream) : launch_tc<BN, 1>(mw, mx, args, stream);
 }
 
 constexpr size_t kFlagBytes = 1024;  // per-CTA partial-ready flags at the start of the workspace
 constexpr int kMinUnitsPerCta = 4;
 
 struct Plan {
-  int bn, ctas, dp;
+  int bn, ch, ctas, dp;
 };
 
-// Token-tile width and scheduling for an M x N x K problem:
-//  * M <= 64 (small decode batches): one token tile; the few weight tiles are
-//    split along K by stream-K so every SM streams weights (partials are small);
-//  * 64 < M <= 256 (decode batches): whole tiles, no K split; the token tile
-//    width (64/96/128/256) is the one whose tile count fills the SMs best;
-//  * M > 256 (prefill): 256-token tiles, stream-K across the SMs.
+// Tile shape and scheduling for an M x N x K problem (rules fitted to B200
+// measurements of the decode and prefill shapes of the Qwen3 family):
+//  * M <= 128: one token tile of BN = M rounded up to 32/64/96/128;
+//    M in (128, 256]: 128-token tiles (two for a 256-sequence decode batch);
+//    M > 256 (prefill): 256-token tiles.
+//  * Whole tiles are dealt round-robin ("data-parallel") when there are at least
+//    half as many tiles as SMs, or when K is short (<= 16 steps) so that a
+//    stream-K fixup would cost more than the idle SMs; otherwise stream-K
+//    splits the tiles x K-steps work evenly over the SMs.
 Plan make_plan(int M, int N, int K, int num_sms) {
+  Plan p{256, (K % kChunk == 0) ? 2 : 1, 1, 0};
+  if (M <= 32) p.bn = 32;
+  else if (M <= 64) p.bn = 64;
+  else if (M <= 96) p.bn = 96;
+  else if (M <= 256) p.bn = 128;
   const int64_t tiles_n = (N + kBM - 1) / kBM;
-  const int64_t KT = (K + kBK - 1) / kBK;
-  Plan p{256, 1, 0};
-  if (M > 64 && M <= 256) {
-    const int cands[4] = {256, 128, 96, 64};
-    double best = -1.0;
-    for (int bn : cands) {
-      const int64_t T = tiles_n * ((M + bn - 1) / bn);
-      const int64_t waves = (T + num_sms - 1) / num_sms;
-      const double eff = (double)T / ((double)waves * num_sms);
-      if (eff > best + 1e-9) {
-        best = eff;
-        p.bn = bn;
-      }
-    }
-    if (best >= 0.85) {
-      const int64_t T = tiles_n * ((M + p.bn - 1) / p.bn);
-      p.dp = 1;
-      p.ctas = (int)(T < num_sms ? T : num_sms);
-      return p;
-    }
-    p.bn = M <= 128 ? 128 : 256;
-  } else if (M <= 64) {
-    p.bn = M <= 32 ? 32 : 64;
+  const int64_t tiles_m = (M + p.bn - 1) / p.bn;
+  const int64_t T = tiles_n * tiles_m;
+  const int64_t KT = (K + kChunk * p.ch - 1) / (kChunk * p.ch);
+  const bool decode = M <= 256 && M > 64;
+  if (decode && (2 * T >= num_sms || KT <= 16)) {
+    p.dp = 1;
+    p.ctas = (int)(T < num_sms ? T : num_sms);
+    return p;
   }
-  const int64_t U = tiles_n * ((M + p.bn - 1) / p.bn) * KT;
-  int64_t g = U / kMinUnitsPerCta;
+  const int64_t waves = (T + num_sms - 1) / num_sms;
+  if (T >= num_sms && (double)T / ((double)waves * num_sms) >= 0.9) {
+    p.dp = 1;
+    p.ctas = num_sms;
+    return p;
+  }
+  int64_t g = T * KT / kMinUnitsPerCta;
   if (g < 1) g = 1;
   if (g > num_sms) g = num_sms;
   if (g > (int64_t)(kFlagBytes / sizeof(int))) g = kFlagBytes / sizeof(int);
@@ -574,12 +674,12 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   if (!p.dp && (gemm_workspace_bytes(M, N, K, num_sms) > workspace_bytes || workspace == nullptr))
     return cudaErrorInvalidValue;
   CUtensorMap mw, mx;
-  if (!make_map(&mw, wq, N, K, kBM) || !make_map(&mx, xq, M, K, bn)) return cudaErrorInvalidValue;
+  if (!make_map(&mw, wq, N, K, kBM, p.ch) || !make_map(&mx, xq, M, K, bn, p.ch)) return cudaErrorInvalidValue;
   GemmArgs args;
   args.M = M;
   args.N = N;
   args.K = K;
-  args.KT = (K + kBK - 1) / kBK;
+  args.KT = (K + kChunk * p.ch - 1) / (kChunk * p.ch);
   args.tiles_m = (M + bn - 1) / bn;
   args.T = (int64_t)((N + kBM - 1) / kBM) * args.tiles_m;
   args.U = args.T * args.KT;
@@ -592,11 +692,12 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   args.flags = p.dp ? nullptr : (int*)workspace;
   args.ws = p.dp ? nullptr : (float*)((char*)workspace + kFlagBytes);
   switch (bn) {
-    case 32: return launch_tc<32>(mw, mx, args, stream);
-    case 64: return launch_tc<64>(mw, mx, args, stream);
-    case 96: return launch_tc<96>(mw, mx, args, stream);
-    case 128: return launch_tc<128>(mw, mx, args, stream);
-    default: return launch_tc<256>(mw, mx, args, stream);
+    case 32: return launch_bn<32>(p.ch, mw, mx, args, stream);
+    case 64: return launch_bn<64>(p.ch, mw, mx, args, stream);
+    case 96: return launch_bn<96>(p.ch, mw, mx, args, stream);
+    case 128: return launch_bn<128>(p.ch, mw, mx, args, stream);
+    case 192: return launch_bn<192>(p.ch, mw, mx, args, stream);
+    default: return launch_bn<256>(p.ch, mw, mx, args, stream);
   }
 }
 

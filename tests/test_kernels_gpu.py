@@ -80,6 +80,8 @@ GEMM_SHAPES = [
     (1, 6144, 4096), (16, 4096, 4096), (64, 24576, 1024), (100, 1024, 3072), (256, 6144, 4096),
     (256, 4096, 12288), (256, 5120, 3200), (300, 2048, 1024), (1024, 4096, 4096), (4096, 6144, 4096),
     (8, 4096, 512), (33, 96, 160),
+    # token tiles of 96 / 192 columns, an odd number of 128-byte K chunks, K % 128 != 0
+    (96, 4096, 4096), (150, 2048, 4096), (200, 384, 1280), (256, 1024, 1040), (129, 640, 4224),
 ]
 
 
