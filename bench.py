@@ -343,6 +343,7 @@ def run_ours(args):
         tp.init_tensor_parallel()
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
     lib = _lib.load()
+    lib.ms_set_pdl(0 if args.no_pdl else 1)
     cfg = qwen3_cfg(args.model)
     reqs = prompts(args.batch, args.prompt_min, args.prompt_max, cfg.vocab_size)
     steps_total = args.warmup + args.steps
@@ -404,6 +405,7 @@ def run_ours(args):
                                f"{int(batch['ctx0'].min())}-{int(batch['ctx0'].max())} growing 1 token/step",
                    "model": f"qwen3-{args.model}", "global_batch": B, "seq_len": int(batch["ctx0"].mean()),
                    "parallelism": f"tp{args.gpus}", "kv_cache": "fp8_e4m3, 256-token pages",
+                   "pdl": not args.no_pdl,
                    "l2": "inputs larger than L2 (weights + KV >> 126 MB); no flush"},
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(d["achieved_gbs"], 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(d["frac"], 4), "traffic": None,
@@ -574,6 +576,8 @@ def main():
     ap.add_argument("--max-batched-tokens", type=int, default=8192)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="launch the library's kernels without programmatic dependent launch")
     ap.add_argument("--kv-blocks", type=int, default=0, help="KV-cache blocks (0: size from free memory)")
     ap.add_argument("--kernel", choices=["decode_attention", "gemm"], default=None,
                     help="time one kernel on synthetic inputs (sweeps / profiling) instead of the model")

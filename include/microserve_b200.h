@@ -48,6 +48,14 @@ const char* ms_last_error(void);
  * library, so it is counted once, at capture). */
 int64_t ms_launch_count(void);
 
+/* Programmatic dependent launch (no reference counterpart; a launch setting of
+ * this library). When enabled (the default) every kernel is launched with
+ * programmatic stream serialization allowed: it may start its prologue (and,
+ * for the GEMM, its weight loads) while the preceding kernel in the stream
+ * finishes, and waits for that kernel before touching any data it could
+ * produce or consume. Returns the previous setting. Process-wide. */
+int ms_set_pdl(int enable);
+
 /* Reads and clears the device status word of the current device. Kernels
  * that wait on barriers give up after a bounded time, record a non-zero code
  * there (1 = tensor-core pipeline timeout, 2 = peer timeout) and return.

@@ -23,6 +23,7 @@ SIGNATURES: dict[str, tuple] = {
     "ms_version": (i32, []),
     "ms_last_error": (C.c_char_p, []),
     "ms_launch_count": (i64, []),
+    "ms_set_pdl": (i32, [i32]),
     "ms_get_device_status": (i32, [C.POINTER(C.c_int), vp]),
     "ms_quantize_rows_fp8": (i32, [vp, i64, i64, i64, vp, vp, vp]),
     "ms_fp8_gemm_workspace_size": (sz, [i64, i64, i64]),

@@ -19,6 +19,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <utility>
 
 #define MS_FP8_MAX 448.0f
 
@@ -45,6 +46,41 @@ extern std::atomic<long long> g_host_launches;
 
 __device__ __forceinline__ void set_device_status(int code) {
   atomicCAS(&g_device_status, 0, code);
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL). Every kernel of the library is launched
+// with programmatic stream serialization allowed, so it may start while the
+// preceding kernel in the stream is still running. Contract for each kernel:
+//  * pdl_wait() before its first access to memory that earlier work in the
+//    stream writes or reads (inputs, outputs, workspaces); only immutable data
+//    (weights, tensor maps) and on-chip state may be touched before it;
+//  * pdl_trigger() once the CTA no longer blocks the next kernel from starting
+//    its own prologue. The next kernel starts when every CTA has triggered or
+//    exited, so all CTAs of this grid are resident by then.
+// Without the launch attribute both are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host: whether launches carry the programmatic-serialization attribute.
+extern std::atomic<int> g_pdl_enabled;
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl_enabled.load(std::memory_order_relaxed) ? 1 : 0;
+  MS_COUNT_LAUNCH();
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------

@@ -8,9 +8,13 @@
 //  * One CTA per (split, kv head, sequence); the G = Hq/Hkv query heads that
 //    share a kv head are processed together so every K/V byte is read once
 //    (the reference re-reads K/V once per query head).
-//  * K and V go straight from HBM to registers with 16-byte loads (no shared
-//    memory), are widened e4m3 -> f16 in registers (exact), and both products
-//    run on the tensor cores with mma.m16n8k16 (f16 in, f32 accumulate):
+//  * Each warp streams its 16-token tiles of K, V and their scales through a
+//    private ring of kStages shared-memory stages with cp.async (16-byte
+//    copies, L2 only), so kStages tiles per warp are in flight without holding
+//    registers; the 16-byte chunks of a row are XOR-swizzled so that both
+//    fragment read patterns below are bank-conflict free. Fragments are
+//    widened e4m3 -> f16 in registers (exact), and both products run on the
+//    tensor cores with mma.m16n8k16 (f16 in, f32 accumulate):
 //        S^T[tok, head] = K[tok, d] . Q^T[d, head]      (M = 16 tokens, N = 8 heads)
 //        O^T[d, head]  += V^T[d, tok] . P'^T[tok, head] (M = 16 of d, N = 8 heads)
 //    The head_dim axis of each product is permuted so that every thread's
@@ -37,6 +41,11 @@ namespace {
 
 constexpr int kD = 128;
 constexpr int kWarps = 4;
+constexpr int kStages = 4;                               // tiles in flight per warp
+constexpr int kTileBytes = 16 * kD;                      // one operand of a 16-token tile
+constexpr int kStageBytes = 2 * kTileBytes + 2 * 16 * 4;  // K, V, k scales, v scales
+constexpr int kSmemBytes = kWarps * kStages * kStageBytes;
+static_assert(kSmemBytes >= (kWarps * 8 * (kD + 4) + 2 * kWarps * 8) * 4, "merge buffers alias the stages");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kPScaleLog2 = 14.f;       // P' scaled into [0, 2^14] for its f16 hi/lo split
 constexpr float kPUnscale = 1.f / 16384.f;
@@ -79,13 +88,22 @@ __device__ __forceinline__ float2 h2_to_f2(uint32_t x) {
   return __half22float2(h);
 }
 
-__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Position of 16-byte chunk j of tile row r: j ^ swz(r). Makes both read
+// patterns conflict free: K reads rows {2p, 2p+1} x chunks {0..3} (or {4..7})
+// per quarter warp, V reads rows {0, 2, 4, 6} (+1, +8) x a chunk pair.
+__device__ __forceinline__ int swz(int r) { return (r & 6) ^ ((r & 1) << 2); }
 
 struct DecodeArgs {
   const __half* q;            // [B, Hq, D]
@@ -102,7 +120,10 @@ struct DecodeArgs {
   float scale_log2;           // softmax_scale * log2(e)
 };
 
-__global__ void __launch_bounds__(kWarps * 32) decode_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, 3) decode_kernel(DecodeArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  pdl_wait();
+  pdl_trigger();
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -135,29 +156,59 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(DecodeArgs a) {
 
   const int64_t tok_stride = (int64_t)a.Hkv * kD;  // bytes between consecutive tokens of a page
   const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
+  unsigned char* wsm = smem + warp * (kStages * kStageBytes);  // this warp's ring
+  const uint32_t wsm_u32 = smem_u32(wsm);
+  const int first = t_begin + warp;
+  const int n_my = first < t_end ? (t_end - first + kWarps - 1) / kWarps : 0;
 
-  for (int tile = t_begin + warp; tile < t_end; tile += kWarps) {
-    const int p0 = tile << 4;
+  // Copy tile number k of this warp (all lanes) into stage k % kStages. The 16
+  // tokens of a tile never cross a page (block_size % 16 == 0), and every tile
+  // starts below L, so its page is in the table and all 16 rows are in memory.
+  auto issue = [&](int k) {
+    const int p0 = (first + k * kWarps) << 4;
     const int page = p0 / a.block_size;
-    const int off = p0 - page * a.block_size;
-    const int64_t phys = bt[page];
-    const int64_t tok0 = phys * a.block_size + off;  // global token slot of row 0 of this tile
-    const uint8_t* kbase = a.k_cache + (tok0 * a.Hkv + kvh) * kD;
-    const uint8_t* vbase = a.v_cache + (tok0 * a.Hkv + kvh) * kD;
-    // K rows g, g+8: bytes [16c, 16c+16) and [64+16c, ...)
-    uint4 k0a = ldg_nc_v4(kbase + g * tok_stride + 16 * c);
-    uint4 k0b = ldg_nc_v4(kbase + g * tok_stride + 64 + 16 * c);
-    uint4 k1a = ldg_nc_v4(kbase + (g + 8) * tok_stride + 16 * c);
-    uint4 k1b = ldg_nc_v4(kbase + (g + 8) * tok_stride + 64 + 16 * c);
-    // V rows 2c, 2c+1, 2c+8, 2c+9: bytes [16g, 16g+16)
-    uint4 v0 = ldg_nc_v4(vbase + (2 * c) * tok_stride + 16 * g);
-    uint4 v1 = ldg_nc_v4(vbase + (2 * c + 1) * tok_stride + 16 * g);
-    uint4 v2 = ldg_nc_v4(vbase + (2 * c + 8) * tok_stride + 16 * g);
-    uint4 v3 = ldg_nc_v4(vbase + (2 * c + 9) * tok_stride + 16 * g);
-    const float ks0 = a.k_scale[(tok0 + g) * a.Hkv + kvh];
-    const float ks1 = a.k_scale[(tok0 + g + 8) * a.Hkv + kvh];
-    const float vs0 = a.v_scale[(tok0 + g) * a.Hkv + kvh];
-    const float vs1 = a.v_scale[(tok0 + g + 8) * a.Hkv + kvh];
+    const int64_t tok0 = (int64_t)__ldg(bt + page) * a.block_size + (p0 - page * a.block_size);
+    const uint8_t* kb = a.k_cache + (tok0 * a.Hkv + kvh) * kD;
+    const uint8_t* vb = a.v_cache + (tok0 * a.Hkv + kvh) * kD;
+    const uint32_t st = wsm_u32 + (uint32_t)((k % kStages) * kStageBytes);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = lane + 32 * i, r = q >> 3, j = q & 7;
+      const uint32_t o = (uint32_t)(r * 128 + ((j ^ swz(r)) << 4));
+      cp_async16(st + o, kb + r * tok_stride + 16 * j);
+      cp_async16(st + kTileBytes + o, vb + r * tok_stride + 16 * j);
+    }
+    const int r = lane & 15;
+    const float* sp = (lane < 16 ? a.k_scale : a.v_scale) + (tok0 + r) * a.Hkv + kvh;
+    cp_async4(st + 2 * kTileBytes + (lane >> 4) * 64 + r * 4, sp);
+  };
+#pragma unroll
+  for (int k = 0; k < kStages; ++k) {
+    if (k < n_my) issue(k);
+    cp_async_commit();  // one group per tile slot, empty or not
+  }
+
+  for (int k = 0; k < n_my; ++k) {
+    cp_async_wait<kStages - 1>();  // this lane's copies of tile k have landed
+    __syncwarp();                  // ... and every other lane's
+    const int p0 = (first + k * kWarps) << 4;
+    const unsigned char* sk = wsm + (k % kStages) * kStageBytes;
+    const unsigned char* sv = sk + kTileBytes;
+    const float* sks = reinterpret_cast<const float*>(sk + 2 * kTileBytes);
+    auto ld = [](const unsigned char* t, int r, int j) {
+      return *reinterpret_cast<const uint4*>(t + r * 128 + ((j ^ swz(r)) << 4));
+    };
+    // K rows g, g+8: chunks c and 4 + c
+    const uint4 k0a = ld(sk, g, c), k0b = ld(sk, g, 4 + c);
+    const uint4 k1a = ld(sk, g + 8, c), k1b = ld(sk, g + 8, 4 + c);
+    // V rows 2c, 2c+1, 2c+8, 2c+9: chunk g
+    uint4 v0 = ld(sv, 2 * c, g), v1 = ld(sv, 2 * c + 1, g);
+    uint4 v2 = ld(sv, 2 * c + 8, g), v3 = ld(sv, 2 * c + 9, g);
+    const float ks0 = sks[g], ks1 = sks[g + 8];
+    const float vs0 = sks[16 + g], vs1 = sks[16 + g + 8];
+    __syncwarp();  // every lane has its fragments: the stage may be refilled
+    if (k + kStages < n_my) issue(k + kStages);
+    cp_async_commit();
     const bool tail = p0 + 16 > L;
     if (tail) {  // zero V rows past the end so stale bytes can never reach the product
       if (p0 + 2 * c >= L) v0 = make_uint4(0, 0, 0, 0);
@@ -191,7 +242,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(DecodeArgs a) {
     // Fold the per-token v scale into the exponent: w = p * v_scale = exp2(s + log2(v_scale) - m),
     // with the running max m taken over s + log2(v_scale), so every weight is in (0, 1] and its
     // f16 hi/lo split (below) keeps ~22 bits. The denominator sums exp2(s - m) in fp32.
-    const float lv0 = lg2(vs0), lv1 = lg2(vs1);
+    const float lv0 = ok0 ? lg2(vs0) : 0.f, lv1 = ok1 ? lg2(vs1) : 0.f;
     const float w0 = s[0] + lv0, w1 = s[1] + lv0, w2 = s[2] + lv1, w3 = s[3] + lv1;
     float tmax0 = fmaxf(w0, w2), tmax1 = fmaxf(w1, w3);
 #pragma unroll
@@ -249,8 +300,11 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(DecodeArgs a) {
     l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], o);
     l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], o);
   }
-  __shared__ float sm_m[kWarps][8], sm_l[kWarps][8];
-  __shared__ float sm_o[kWarps][8][kD + 4];
+  cp_async_wait<0>();
+  __syncthreads();  // every warp is done with its ring: reuse it for the merge
+  float(*sm_o)[8][kD + 4] = reinterpret_cast<float(*)[8][kD + 4]>(smem);
+  float(*sm_m)[8] = reinterpret_cast<float(*)[8]>(smem + sizeof(float) * kWarps * 8 * (kD + 4));
+  float(*sm_l)[8] = sm_m + kWarps;
   if (g == 0) {
     sm_m[warp][2 * c] = m_run[0];
     sm_m[warp][2 * c + 1] = m_run[1];
@@ -309,6 +363,8 @@ __global__ void __launch_bounds__(kD) decode_merge_kernel(const float* __restric
                                                           const float* __restrict__ ws_ml,
                                                           const int32_t* __restrict__ seqlens, int Hq, int splits,
                                                           __half* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.y, hq = blockIdx.x, d = threadIdx.x;
   const int64_t row0 = ((int64_t)b * Hq + hq) * splits;
   float M = -INFINITY;
@@ -368,14 +424,16 @@ cudaError_t launch_decode_attention(const void* q, const void* k_cache, const vo
   a.splits = splits;
   a.scale_log2 = softmax_scale * kLog2e;
   dim3 grid(splits, Hkv, B);
-  decode_kernel<<<grid, kWarps * 32, 0, stream>>>(a);
-  MS_COUNT_LAUNCH();
-  if (splits > 1) {
-    dim3 g2(Hq, B);
-    decode_merge_kernel<<<g2, kD, 0, stream>>>(a.ws_o, a.ws_ml, seqlens, Hq, splits, (__half*)out);
-    MS_COUNT_LAUNCH();
-  }
-  return cudaGetLastError();
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  cudaError_t e = launch_kernel(decode_kernel, grid, dim3(kWarps * 32), kSmemBytes, stream, a);
+  if (e != cudaSuccess || splits <= 1) return e;
+  return launch_kernel(decode_merge_kernel, dim3(Hq, B), dim3(kD), 0, stream, (const float*)a.ws_o,
+                       (const float*)a.ws_ml, seqlens, Hq, splits, (__half*)out);
 }
 
 // ---------------------------------------------------------------------------

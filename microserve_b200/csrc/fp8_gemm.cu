@@ -195,11 +195,6 @@ __device__ __forceinline__ int k_rotation(const GemmArgs& a, int64_t t, int kb, 
   return (int)(((t / a.tiles_m) * 5) % (ke - kb));
 }
 
-// Programmatic dependent launch: wait for the preceding grid's results / let the
-// next grid start its prologue. Both are no-ops when the launch did not opt in.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
 // Persistent GEMM, data-parallel or stream-K. In stream-K mode the U = tiles *
 // KT work units (one K step of one 128 x BN output tile) are split evenly over
 // G CTAs; each CTA walks its contiguous range tile by tile ("segments"). A
@@ -473,6 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void fp8_gemm_simt_kernel(const uint8_t* __restrict__ xq, const uint8_t* __restrict__ wq, int M, int N,
                                      int K, const float* __restrict__ sx, const float* __restrict__ sw,
                                      const __half* __restrict__ bias, __half* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   const int m = blockIdx.y;
   if (n >= N) return;
@@ -575,21 +572,11 @@ cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const GemmAr
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  // Stream-K owners wait for later CTAs' partials, so every CTA must be
-  // resident at once: a cooperative launch of at most one CTA per SM.
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(args.G);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = args.dp ? 0 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<BN, CH>, mw, mx, args);
-  MS_COUNT_LAUNCH();
-  return e;
+  // Stream-K owners wait for later CTAs' partials, so all G <= SM-count CTAs
+  // (one per SM) must become resident. The preceding grid never waits on this
+  // one, so its SMs free up; the next grid cannot start before every CTA here
+  // has triggered (after issuing its last load), i.e. before all are resident.
+  return launch_kernel(fp8_gemm_kernel<BN, CH>, dim3(args.G), dim3(kThreads), C::kSmemBytes, stream, mw, mx, args);
 }
 
 template <int BN>
@@ -664,10 +651,8 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   if (M == 0 || N == 0) return cudaSuccess;
   if (K % 16 != 0) {
     dim3 grid((N + 127) / 128, M);
-    fp8_gemm_simt_kernel<<<grid, 128, 0, stream>>>((const uint8_t*)xq, (const uint8_t*)wq, M, N, K, sx, sw,
-                                                    (const __half*)bias, (__half*)y);
-    MS_COUNT_LAUNCH();
-    return cudaGetLastError();
+    return launch_kernel(fp8_gemm_simt_kernel, grid, dim3(128), 0, stream, (const uint8_t*)xq, (const uint8_t*)wq, M,
+                         N, K, sx, sw, (const __half*)bias, (__half*)y);
   }
   const Plan p = make_plan(M, N, K, num_sms);
   const int bn = p.bn;

@@ -42,6 +42,8 @@ __global__ void __launch_bounds__(256) store_kv_fp8_kernel(const __half* __restr
                                                            uint8_t* __restrict__ k_cache,
                                                            uint8_t* __restrict__ v_cache, float* __restrict__ k_scale,
                                                            float* __restrict__ v_scale) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t item = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (item >= T * kv_heads) return;
   const int64_t t = item / kv_heads;
@@ -117,6 +119,8 @@ __device__ __forceinline__ void head_rope(float (&x)[4], const __half* __restric
 }
 
 __global__ void __launch_bounds__(256) qkv_post_kernel(QkvPostArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int heads = a.q_heads + 2 * a.kv_heads;
   const int hd = blockIdx.y * 8 + (threadIdx.x >> 5);
   if (hd >= heads) return;
@@ -160,10 +164,8 @@ cudaError_t launch_store_kv_fp8(const void* k, const void* v, int64_t T, int kv_
   if (head_dim != kHeadDim) return cudaErrorInvalidValue;
   if (T == 0) return cudaSuccess;
   const int64_t items = T * kv_heads;
-  store_kv_fp8_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream>>>(
-      (const __half*)k, (const __half*)v, T, kv_heads, slots, (uint8_t*)k_cache, (uint8_t*)v_cache, k_scale, v_scale);
-  MS_COUNT_LAUNCH();
-  return cudaGetLastError();
+  return launch_kernel(store_kv_fp8_kernel, dim3((unsigned)((items + 7) / 8)), dim3(256), 0, stream, (const __half*)k,
+                       (const __half*)v, T, kv_heads, slots, (uint8_t*)k_cache, (uint8_t*)v_cache, k_scale, v_scale);
 }
 
 cudaError_t launch_qkv_post(const void* qkv, int64_t T, int q_heads, int kv_heads, int head_dim, const void* q_norm_w,
@@ -193,9 +195,7 @@ cudaError_t launch_qkv_post(const void* qkv, int64_t T, int q_heads, int kv_head
   a.v_scale = v_scale;
   const int heads = q_heads + 2 * kv_heads;
   dim3 grid((unsigned)T, (unsigned)((heads + 7) / 8));
-  qkv_post_kernel<<<grid, 256, 0, stream>>>(a);
-  MS_COUNT_LAUNCH();
-  return cudaGetLastError();
+  return launch_kernel(qkv_post_kernel, grid, dim3(256), 0, stream, a);
 }
 
 }  // namespace ms

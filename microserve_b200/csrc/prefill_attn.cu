@@ -90,6 +90,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(PrefillArgs a) {
   __shared__ __align__(128) unsigned char sQ[kRows * 256];
   __shared__ __align__(128) unsigned char sK[kKeys * 256];
   __shared__ __align__(128) unsigned char sV[kKeys * 256];
+  pdl_wait();
+  pdl_trigger();
 
   const int kvh = blockIdx.y;
   const int G = a.Hq / a.Hkv;
@@ -339,12 +341,8 @@ cudaError_t launch_prefill_attention(bool paged, const void* q, const void* k16,
   a.max_blocks = max_blocks;
   a.scale_log2 = softmax_scale * kLog2e;
   dim3 grid(blocks, Hkv);
-  if (paged)
-    prefill_kernel<true><<<grid, 128, 0, stream>>>(a);
-  else
-    prefill_kernel<false><<<grid, 128, 0, stream>>>(a);
-  MS_COUNT_LAUNCH();
-  return cudaGetLastError();
+  return paged ? launch_kernel(prefill_kernel<true>, grid, dim3(128), 0, stream, a)
+               : launch_kernel(prefill_kernel<false>, grid, dim3(128), 0, stream, a);
 }
 
 }  // namespace ms

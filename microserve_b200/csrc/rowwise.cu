@@ -53,6 +53,8 @@ __global__ void __launch_bounds__(kRowThreads) quantize_rows_kernel(const __half
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __half* row = reinterpret_cast<__half*>(smem_raw);
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t m = blockIdx.x;
   const __half* xr = x + m * ldx;
   float amax = 0.f;
@@ -96,6 +98,8 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(const __half* __re
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __half* row = reinterpret_cast<__half*>(smem_raw);
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t m = blockIdx.x;
   const int64_t base = m * (int64_t)H;
   float ss = 0.f;
@@ -149,6 +153,8 @@ __global__ void __launch_bounds__(kRowThreads) silu_mul_kernel(const __half* __r
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __half* row = reinterpret_cast<__half*>(smem_raw);
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t m = blockIdx.x;
   const __half* g = gu + m * (int64_t)(2 * I);
   const __half* u = g + I;
@@ -191,17 +197,14 @@ cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t M, int K, v
   if (vec) {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(quantize_rows_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    quantize_rows_kernel<true><<<(unsigned)M, row_threads(K), smem, stream>>>((const __half*)x, ldx, K,
-                                                                              (uint8_t*)xq, sx);
-    MS_COUNT_LAUNCH();
+    return launch_kernel(quantize_rows_kernel<true>, dim3((unsigned)M), dim3(row_threads(K)), smem, stream,
+                         (const __half*)x, ldx, K, (uint8_t*)xq, sx);
   } else {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(quantize_rows_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    quantize_rows_kernel<false><<<(unsigned)M, row_threads(K), smem, stream>>>((const __half*)x, ldx, K,
-                                                                               (uint8_t*)xq, sx);
-    MS_COUNT_LAUNCH();
+    return launch_kernel(quantize_rows_kernel<false>, dim3((unsigned)M), dim3(row_threads(K)), smem, stream,
+                         (const __half*)x, ldx, K, (uint8_t*)xq, sx);
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launch_rmsnorm(const void* x, const void* residual, const void* weight, int64_t M, int H, float eps,
@@ -211,11 +214,9 @@ cudaError_t launch_rmsnorm(const void* x, const void* residual, const void* weig
   size_t smem = (size_t)H * 2;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  rmsnorm_kernel<<<(unsigned)M, row_threads(H), smem, stream>>>(
-      (const __half*)x, (const __half*)residual, (const __half*)weight, H, eps, (__half*)residual_out, (__half*)y,
-      (uint8_t*)yq, sy);
-  MS_COUNT_LAUNCH();
-  return cudaGetLastError();
+  return launch_kernel(rmsnorm_kernel, dim3((unsigned)M), dim3(row_threads(H)), smem, stream, (const __half*)x,
+                       (const __half*)residual, (const __half*)weight, H, eps, (__half*)residual_out, (__half*)y,
+                       (uint8_t*)yq, sy);
 }
 
 cudaError_t launch_silu_mul(const void* gu, int64_t M, int I, void* out, void* aq, float* sa, cudaStream_t stream) {
@@ -224,10 +225,8 @@ cudaError_t launch_silu_mul(const void* gu, int64_t M, int I, void* out, void* a
   size_t smem = (size_t)I * 2;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(silu_mul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  silu_mul_kernel<<<(unsigned)M, row_threads(I), smem, stream>>>((const __half*)gu, I, (__half*)out,
-                                                                  (uint8_t*)aq, sa);
-  MS_COUNT_LAUNCH();
-  return cudaGetLastError();
+  return launch_kernel(silu_mul_kernel, dim3((unsigned)M), dim3(row_threads(I)), smem, stream, (const __half*)gu, I,
+                       (__half*)out, (uint8_t*)aq, sa);
 }
 
 }  // namespace ms

@@ -4,4 +4,5 @@
 namespace ms {
 __device__ int g_device_status = 0;
 std::atomic<long long> g_host_launches{0};
+std::atomic<int> g_pdl_enabled{1};
 }  // namespace ms
