@@ -1,8 +1,10 @@
 // Row-wise kernels of the FP8 decoder layer: per-row FP8 quantisation,
 // (residual +) RMSNorm with an optional FP8 epilogue, SiLU*mul with an
-// optional FP8 epilogue. All are HBM-bound; each CTA owns one row, stages the
-// row's fp16 values in shared memory (so the amax needed by the FP8 scale is
-// known before any byte is written) and writes 16-byte vectors.
+// optional FP8 epilogue. All are HBM-bound; each CTA owns one row and copies
+// all of its inputs into shared memory with cp.async up front (every byte of
+// the row in flight at once: these kernels are short and latency-bound), so the
+// amax needed by the FP8 scale is known before any byte is written; outputs are
+// written as 16-byte vectors.
 //
 // Reference semantics followed (microserve, file:line):
 //   quantize rows      layers/fp8_linear.py:14-23   (and the offline weight quant :51-54)
@@ -15,7 +17,21 @@
 namespace ms {
 namespace {
 
-constexpr int kRowThreads = 256;
+constexpr int kRowThreads = 512;
+
+// Copy n16 16-byte chunks global -> shared with cp.async (L2 only), spread over
+// the block; completes with cp_async_wait_all().
+__device__ __forceinline__ void stage_row(void* dst_smem, const void* src, int n16) {
+  const uint32_t d = smem_u32(dst_smem);
+  const char* sp = static_cast<const char*>(src);
+  for (int v = threadIdx.x; v < n16; v += blockDim.x)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + 16u * v), "l"(sp + (size_t)16 * v)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+}
 
 struct alignas(16) H8 {
   __half2 h[4];
@@ -59,14 +75,15 @@ __global__ void __launch_bounds__(kRowThreads) quantize_rows_kernel(const __half
   const __half* xr = x + m * ldx;
   float amax = 0.f;
   if (kVec) {
+    stage_row(row, xr, K / 8);
+    cp_async_wait_all();
     for (int v = threadIdx.x; v < K / 8; v += blockDim.x) {
-      H8 a = *reinterpret_cast<const H8*>(xr + v * 8);
+      H8 a = *reinterpret_cast<const H8*>(row + v * 8);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float2 f = __half22float2(a.h[j]);
         amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
       }
-      *reinterpret_cast<H8*>(row + v * 8) = a;
     }
   } else {
     for (int k = threadIdx.x; k < K; k += blockDim.x) {
@@ -102,11 +119,17 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(const __half* __re
   pdl_trigger();
   const int64_t m = blockIdx.x;
   const int64_t base = m * (int64_t)H;
+  __half* rres = row + H;     // residual row
+  __half* wrow = row + 2 * H;  // weight
+  stage_row(row, x + base, H / 8);
+  if (residual != nullptr) stage_row(rres, residual + base, H / 8);
+  stage_row(wrow, weight, H / 8);
+  cp_async_wait_all();
   float ss = 0.f;
   for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
-    H8 a = *reinterpret_cast<const H8*>(x + base + v * 8);
+    H8 a = *reinterpret_cast<const H8*>(row + v * 8);
     if (residual != nullptr) {
-      H8 r = *reinterpret_cast<const H8*>(residual + base + v * 8);
+      H8 r = *reinterpret_cast<const H8*>(rres + v * 8);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float2 fa = __half22float2(a.h[j]);
@@ -114,20 +137,20 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(const __half* __re
         a.h[j] = __floats2half2_rn(fa.x + fr.x, fa.y + fr.y);
       }
       *reinterpret_cast<H8*>(residual_out + base + v * 8) = a;
+      *reinterpret_cast<H8*>(row + v * 8) = a;
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float2 f = __half22float2(a.h[j]);
       ss += f.x * f.x + f.y * f.y;
     }
-    *reinterpret_cast<H8*>(row + v * 8) = a;
   }
   ss = block_reduce<false>(ss, red);
   const float inv = rsqrtf(ss / (float)H + eps);
   float amax = 0.f;
   for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
     H8 a = *reinterpret_cast<const H8*>(row + v * 8);
-    H8 w = *reinterpret_cast<const H8*>(weight + v * 8);
+    H8 w = *reinterpret_cast<const H8*>(wrow + v * 8);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float2 f = __half22float2(a.h[j]);
@@ -156,12 +179,13 @@ __global__ void __launch_bounds__(kRowThreads) silu_mul_kernel(const __half* __r
   pdl_wait();
   pdl_trigger();
   const int64_t m = blockIdx.x;
-  const __half* g = gu + m * (int64_t)(2 * I);
-  const __half* u = g + I;
+  __half* urow = row + I;
+  stage_row(row, gu + m * (int64_t)(2 * I), I / 4);  // gate and up halves are contiguous
+  cp_async_wait_all();
   float amax = 0.f;
   for (int v = threadIdx.x; v < I / 8; v += blockDim.x) {
-    H8 a = *reinterpret_cast<const H8*>(g + v * 8);
-    H8 b = *reinterpret_cast<const H8*>(u + v * 8);
+    H8 a = *reinterpret_cast<const H8*>(row + v * 8);
+    H8 b = *reinterpret_cast<const H8*>(urow + v * 8);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float2 fa = __half22float2(a.h[j]);
@@ -180,6 +204,16 @@ __global__ void __launch_bounds__(kRowThreads) silu_mul_kernel(const __half* __r
   if (threadIdx.x == 0) sa[m] = scale;
 }
 
+// Opt a kernel in to the largest dynamic shared memory these launchers request
+// (200 KB), once per kernel (a function-local static at each call site); the
+// default 48 KB limit also counts the static reduction buffer.
+#define ALLOW_BIG_SMEM(kernel)                                                                        \
+  do {                                                                                                \
+    static const cudaError_t set_once =                                                               \
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);       \
+    (void)set_once;                                                                                   \
+  } while (0)
+
 inline int row_threads(int K) {
   int t = (K + 7) / 8;
   t = (t + 31) / 32 * 32;
@@ -195,13 +229,11 @@ cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t M, int K, v
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   const bool vec = (K % 16 == 0) && (ldx % 8 == 0) && (((uintptr_t)x & 15) == 0) && (((uintptr_t)xq & 15) == 0);
   if (vec) {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(quantize_rows_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ALLOW_BIG_SMEM(quantize_rows_kernel<true>);
     return launch_kernel(quantize_rows_kernel<true>, dim3((unsigned)M), dim3(row_threads(K)), smem, stream,
                          (const __half*)x, ldx, K, (uint8_t*)xq, sx);
   } else {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(quantize_rows_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ALLOW_BIG_SMEM(quantize_rows_kernel<false>);
     return launch_kernel(quantize_rows_kernel<false>, dim3((unsigned)M), dim3(row_threads(K)), smem, stream,
                          (const __half*)x, ldx, K, (uint8_t*)xq, sx);
   }
@@ -210,10 +242,9 @@ cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t M, int K, v
 cudaError_t launch_rmsnorm(const void* x, const void* residual, const void* weight, int64_t M, int H, float eps,
                            void* residual_out, void* y, void* yq, float* sy, cudaStream_t stream) {
   if (M == 0) return cudaSuccess;
-  if (H % 16 != 0 || H * 2 > 200 * 1024) return cudaErrorInvalidValue;
-  size_t smem = (size_t)H * 2;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (H % 16 != 0 || H * 6 > 200 * 1024) return cudaErrorInvalidValue;
+  size_t smem = (size_t)H * 6;  // x, residual, weight
+  ALLOW_BIG_SMEM(rmsnorm_kernel);
   return launch_kernel(rmsnorm_kernel, dim3((unsigned)M), dim3(row_threads(H)), smem, stream, (const __half*)x,
                        (const __half*)residual, (const __half*)weight, H, eps, (__half*)residual_out, (__half*)y,
                        (uint8_t*)yq, sy);
@@ -221,10 +252,9 @@ cudaError_t launch_rmsnorm(const void* x, const void* residual, const void* weig
 
 cudaError_t launch_silu_mul(const void* gu, int64_t M, int I, void* out, void* aq, float* sa, cudaStream_t stream) {
   if (M == 0) return cudaSuccess;
-  if (I % 16 != 0 || I * 2 > 200 * 1024) return cudaErrorInvalidValue;
-  size_t smem = (size_t)I * 2;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(silu_mul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (I % 16 != 0 || I * 4 > 200 * 1024) return cudaErrorInvalidValue;
+  size_t smem = (size_t)I * 4;  // gate, up
+  ALLOW_BIG_SMEM(silu_mul_kernel);
   return launch_kernel(silu_mul_kernel, dim3((unsigned)M), dim3(row_threads(I)), smem, stream, (const __half*)gu, I,
                        (__half*)out, (uint8_t*)aq, sa);
 }
