@@ -16,8 +16,11 @@ e2e: the full config-3 job through LLMEngine (add 256 requests of 512 output
   tokens, step() until idle): prompts/metadata go host->device from pinned
   memory and sampled tokens come back every step. tok/s = output tokens /
   elapsed, plus ITL p50 (consecutive token-timestamp deltas).
-roofline: the dominant kernel of the decode step, timed alone on the step's
-  own inputs with CUDA events; algorithmic bytes per launch over that time.
+roofline: the kernel class with the largest share of the decode step (the four
+  FP8 GEMMs of a layer, else the decode attention), each launch timed alone on the
+  step's own inputs with CUDA events (CUDA-graph replay); algorithmic bytes over
+  that time; `traffic` = DRAM bytes of the same launches from ncu captures
+  (profiles/roofline_traffic.json).
 cpu_baseline: the CPU oracle (a restatement of the reference's FP8 path) on
   the host cores for one decoder layer of the same decode step, scaled to
   the full model.
@@ -78,39 +81,66 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region (median SM clock, throttle reasons)."""
+    """nvidia-smi samples taken DURING the timed region (median SM clock, throttle reasons).
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
+    The sampler process is started and confirmed running (first line read)
+    before the region opens; a reader thread timestamps every line, and only
+    lines that arrive between mark_start() and mark_end() count."""
+
+    def __init__(self, index: int, period_ms: int = 25):
+        self.index, self.period_ms = index, period_ms
+        self.proc, self.lines, self.t0, self.t1 = None, [], None, None
+        self._stamped = []
 
     def __enter__(self):
+        import threading
         q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", str(self.period_ms)],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (FileNotFoundError, OSError):
             self.proc = None
+            return self
+        first = threading.Event()
+
+        def reader():
+            for line in self.proc.stdout:
+                self._stamped.append((time.monotonic(), line))
+                first.set()
+            first.set()
+        self._thread = threading.Thread(target=reader, daemon=True)
+        self._thread.start()
+        first.wait(timeout=10)
         return self
 
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_end(self):
+        self.t1 = time.monotonic()
+
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        if self.proc is None:
+            return
+        if self.t1 is not None:  # let the sample in flight at the end of the region arrive
+            time.sleep(2 * self.period_ms / 1000)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self._thread.join(timeout=5)
+        t0 = self.t0 if self.t0 is not None else 0.0
+        t1 = (self.t1 if self.t1 is not None else time.monotonic()) + 1.5 * self.period_ms / 1000
+        self.lines = [l for t, l in self._stamped if t0 <= t <= t1 and l.strip()]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
+        for l in self.lines:
             f = [x.strip() for x in l.split(",")]
             try:
                 sm.append(float(f[0]))
@@ -284,6 +314,41 @@ def kernel_rooflines(engine, batch, step_idx, hbm_peak):
     return res
 
 
+GEMM_CLASS = ("qkv_proj", "o_proj", "gate_up_proj", "down_proj")
+
+
+def measured_traffic():
+    """DRAM bytes from ncu captures of the same kernels (profiles/roofline_traffic.json)."""
+    path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def dominant_roofline(kern, hbm_peak, batch, gpus):
+    """Roofline of the kernel class with the largest share of the decode step: the
+    four FP8 GEMMs of a layer (one class, weights streamed once each) or the decode
+    attention. achieved = algorithmic bytes / CUDA-event time of the launches."""
+    gemm_s = sum(kern[k]["seconds"] for k in GEMM_CLASS)
+    gemm_b = sum(kern[k]["bytes"] for k in GEMM_CLASS)
+    attn = kern["decode_attention"]
+    traffic = measured_traffic()
+    if gemm_s >= attn["seconds"]:
+        name, byts, secs = "fp8_gemm (qkv+o+gate_up+down of one layer)", gemm_b, gemm_s
+        t = traffic.get(f"fp8_gemm_layer_b{batch}_tp{gpus}")
+        tr = int(t["dram_bytes"]) if t else None
+    else:
+        name, byts, secs = "decode_attention", attn["bytes"], attn["seconds"]
+        r = traffic.get("decode_attention_dram_per_algorithmic_byte")
+        tr = int(attn["bytes"] * r["ratio"]) if r else None
+    ach = byts / secs / 1e9
+    return {"bound": "hbm", "kernel": name, "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(ach / hbm_peak, 4), "traffic": tr, "algorithmic_bytes": int(byts),
+            "us": round(secs * 1e6, 2)}
+
+
 @torch.inference_mode()
 def cpu_baseline_layer(engine, batch, step_idx, layers_total, threads=None):
     """Oracle decode of ONE decoder layer for the whole batch on the host cores, scaled
@@ -313,20 +378,26 @@ def cpu_baseline_layer(engine, batch, step_idx, layers_total, threads=None):
     cos, sin = O.rope_tables(HEAD_DIM, int(pos.max()) + 1, 1e6)
     hidden = torch.randn(B, model.config.hidden_size, dtype=torch.float16)
     residual = torch.randn_like(hidden)
-    t0 = time.perf_counter()
-    O.decoder_layer(lw, pos, hidden, residual, Hq=a.num_heads, Hkv=a.num_kv_heads, D=HEAD_DIM, eps=1e-6,
-                    cos_cache=cos, sin_cache=sin, mode="decode", caches=caches, slots=slots,
-                    seqlens=(pos + 1), block_tables=bt_local)
-    t_layer = time.perf_counter() - t0
     head = model.lm_head.weight.cpu()
-    t1 = time.perf_counter()
-    (hidden[:16].float() @ head.float().T).half()
-    t_head = (time.perf_counter() - t1) * B / 16
+    # repeat the sampled layer (and the 16-row LM head sample) until ~10 s of CPU work
+    layer_t, head_t = [], []
+    t_start = time.perf_counter()
+    while len(layer_t) < 2 or (time.perf_counter() - t_start < 10.0 and len(layer_t) < 50):
+        t0 = time.perf_counter()
+        O.decoder_layer(lw, pos, hidden, residual, Hq=a.num_heads, Hkv=a.num_kv_heads, D=HEAD_DIM, eps=1e-6,
+                        cos_cache=cos, sin_cache=sin, mode="decode", caches=caches, slots=slots,
+                        seqlens=(pos + 1), block_tables=bt_local)
+        layer_t.append(time.perf_counter() - t0)
+        t1 = time.perf_counter()
+        (hidden[:16].float() @ head.float().T).half()
+        head_t.append((time.perf_counter() - t1) * B / 16)
+    t_layer, t_head = statistics.median(layer_t), statistics.median(head_t)
     per_step = t_layer * layers_total + t_head
     return dict(value=B / per_step, unit="tok/s", cores=torch.get_num_threads(), kind="port",
                 sample=f"1 of {layers_total} decoder layers of one B={B} decode step (+ LM head on 16 rows), "
-                       f"scaled to the full model; oracle/fp8_decoder.py on {torch.get_num_threads()} threads",
-                seconds_sampled=t_layer + (time.perf_counter() - t1))
+                       f"median of {len(layer_t)} repetitions, scaled to the full model; "
+                       f"oracle/fp8_decoder.py on {torch.get_num_threads()} threads",
+                seconds_sampled=round(time.perf_counter() - t_start, 2))
 
 
 def run_ours(args):
@@ -370,11 +441,13 @@ def run_ours(args):
     end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         torch.cuda.nvtx.range_push("decode_timed")
+        clocks.mark_start()
         start.record()
         for i in range(args.warmup, steps_total):
             step(i)
         end.record()
         torch.cuda.synchronize()
+        clocks.mark_end()
         torch.cuda.nvtx.range_pop()
     elapsed = max_over_ranks(start.elapsed_time(end) / 1e3)
     assert lib.ms_launch_count() == launches_before, "graph replay must not call the library"
@@ -384,8 +457,7 @@ def run_ours(args):
 
     kern = kernel_rooflines(engine, batch, args.warmup, hbm_peak)
     L = cfg.num_hidden_layers
-    dominant = max(kern, key=lambda k: kern[k]["seconds"] * kern[k]["per_layer"])
-    d = kern[dominant]
+    roof = dominant_roofline(kern, hbm_peak, B, args.gpus)
     status = _lib.device_status()
 
     # algorithmic bytes of the whole decode step (per GPU) for context
@@ -407,10 +479,8 @@ def run_ours(args):
                    "parallelism": f"tp{args.gpus}", "kv_cache": "fp8_e4m3, 256-token pages",
                    "pdl": not args.no_pdl,
                    "l2": "inputs larger than L2 (weights + KV >> 126 MB); no flush"},
-        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(d["achieved_gbs"], 1),
-                     "peak": hbm_peak, "unit": "GB/s", "frac": round(d["frac"], 4), "traffic": None,
-                     "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                     else "fallback 6650 GB/s"},
+        "roofline": dict(roof, peak_kind=f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6650 GB/s"),
         "kernels": {k: {"us": round(v["seconds"] * 1e6, 2), "GBps": round(v["achieved_gbs"], 1),
                         "frac": round(v["frac"], 4)} for k, v in kern.items()},
         "step_roofline": {"algorithmic_bytes": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
@@ -424,9 +494,30 @@ def run_ours(args):
         line["cpu_baseline"] = cpu_baseline_layer(engine, batch, args.warmup, L)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    del step
     engine.runner.release_graphs()
-    if torch.distributed.is_initialized():
-        torch.distributed.destroy_process_group()
+    shutdown_distributed()
+
+
+def shutdown_distributed(limit_s: float = 60.0) -> None:
+    """Barrier, then destroy the process group, bounded: a teardown that does not
+    finish within limit_s ends the process (the result line is already printed)."""
+    if not torch.distributed.is_initialized():
+        return
+    import threading
+    done = threading.Event()
+
+    def teardown():
+        try:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        finally:
+            done.set()
+    threading.Thread(target=teardown, daemon=True).start()
+    if not done.wait(limit_s):
+        print("bench: process-group teardown did not finish; exiting", file=sys.stderr, flush=True)
+        sys.stdout.flush()
+        os._exit(0)
 
 
 # ------------------------------------------------------------------------ reference

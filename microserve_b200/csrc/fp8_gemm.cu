@@ -48,7 +48,8 @@ struct GemmArgs {
   int64_t T;    // output tiles
   int64_t U;    // work units = tiles * KT
   int G;        // CTAs (persistent, one per SM at most)
-  int dp;       // 1: whole tiles round-robin (no K split); 0: stream-K
+  int dp;       // 1: whole tiles round-robin (no K split); 0: stream-K or split-K
+  int splits;   // split-K: CTAs per tile (CTA c = tile c / splits, K part c % splits); 0 otherwise
   const float* sx;
   const float* sw;
   const __half* bias;
@@ -166,11 +167,20 @@ __device__ __forceinline__ int64_t unit_begin(int64_t c, int64_t U, int G) { ret
 struct SegIter {
   int64_t u, u_end, t_dp;
   int64_t T;
-  int KT, G, dp;
-  __device__ SegIter(const GemmArgs& a, int cta)
-      : u(unit_begin(cta, a.U, a.G)), u_end(unit_begin(cta + 1, a.U, a.G)), t_dp(cta), T(a.T), KT(a.KT),
-        G(a.G), dp(a.dp) {}
+  int KT, G, dp, splits, cta;
+  __device__ SegIter(const GemmArgs& a, int cta_)
+      : u(unit_begin(cta_, a.U, a.G)), u_end(unit_begin(cta_ + 1, a.U, a.G)), t_dp(cta_), T(a.T), KT(a.KT),
+        G(a.G), dp(a.dp), splits(a.splits), cta(cta_) {}
   __device__ bool next(int64_t& t, int& kb, int& ke) {
+    if (splits > 0) {  // one segment: K part (cta % splits) of tile cta / splits
+      if (t_dp < 0) return false;
+      t = cta / splits;
+      const int j = cta % splits;
+      kb = (int)((int64_t)j * KT / splits);
+      ke = (int)((int64_t)(j + 1) * KT / splits);
+      t_dp = -1;
+      return true;
+    }
     if (dp) {
       if (t_dp >= T) return false;
       t = t_dp;
@@ -193,6 +203,97 @@ struct SegIter {
 __device__ __forceinline__ int k_rotation(const GemmArgs& a, int64_t t, int kb, int ke) {
   if (!a.dp || ke - kb < 2) return 0;
   return (int)(((t / a.tiles_m) * 5) % (ke - kb));
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Split-K epilogue (all 128 epilogue threads of a CTA). The `splits` CTAs of a
+// tile each hold a K part in TMEM. Every CTA stores its fp32 partial
+// (column-major [BN][128], 8 KB per 16 columns) to its workspace slot and
+// arrives on the tile's counter; once all parts are in, each CTA reduces a
+// different slice of 16-column chunks: one thread brings that slice of every
+// partial into shared memory with bulk copies (the pipeline stages are idle:
+// one tile per CTA), then each thread sums its row over the parts in a fixed
+// order, applies the dequant scales and stores. The counter goes to 2 *
+// splits (arrive, then done) and the last CTA resets it to zero.
+template <int BN, int CH>
+__device__ __forceinline__ void split_epilogue(const GemmArgs& args, uint32_t acc, int64_t t, int m0, int cols, int n,
+                                               bool n_ok, float swn, float bn, const float* sx, float* my_ws,
+                                               unsigned char* smem, uint64_t* red_full, uint64_t* acc_empty, int et,
+                                               int row) {
+  using C = Cfg<BN, CH>;
+  const int S = args.splits;
+  for (int c0 = 0; c0 < BN; c0 += 16) {
+    float v[16];
+    tmem_ld16(acc + (uint32_t)c0, v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) my_ws[(int64_t)(c0 + j) * kBM + row] = v[j];
+  }
+  // These stores are read back by bulk copies (the async proxy), in this CTA and
+  // in the tile's other CTAs: order them for that proxy, then GPU-wide.
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  __threadfence();
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  mbar_arrive(acc_empty);
+  constexpr int kChunks = BN / 16;
+  const int part = (int)(blockIdx.x % S);
+  const int per = (kChunks + S - 1) / S;
+  const int q0 = min(kChunks, part * per), q1 = min(kChunks, q0 + per);
+  int* cnt = args.flags + t;
+  epi_sync();  // every partial store of this CTA precedes the release below
+  if (et == 0) {
+    atomicAdd(cnt, 1);
+    const uint64_t t0 = global_ns();
+    uint32_t spins = 0;
+    while (ld_acquire(cnt) < S) {
+      if ((++spins & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+        set_device_status(kStatusMbarTimeout);
+        break;
+      }
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // the bulk copies below read other CTAs' stores
+    const uint32_t bytes = (uint32_t)(S * (q1 - q0)) * 16u * kBM * 4u;
+    mbar_arrive_expect_tx(red_full, bytes);
+    const float* base = args.ws + (int64_t)(t * S) * BN * kBM;
+    for (int p = 0; p < S; ++p)
+      for (int q = q0; q < q1; ++q)
+        bulk_g2s(smem_u32(smem + (size_t)(p * per + (q - q0)) * 16 * kBM * 4),
+                 base + (int64_t)p * BN * kBM + (int64_t)q * 16 * kBM, 16u * kBM * 4u, red_full);
+  }
+  static_assert(C::kStages * C::kStageBytes >= (kChunks + 8) * 16 * kBM * 4, "split-K slices fit the stages");
+  const bool ok = mbar_wait(red_full, 0);
+  const float* red = reinterpret_cast<const float*>(smem);
+  for (int q = q0; ok && q < q1; ++q) {
+    const int c0 = q * 16;
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+    for (int p = 0; p < S; ++p) {
+      const float* src = red + (size_t)(p * per + (q - q0)) * 16 * kBM + row;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] += src[j * kBM];
+    }
+    if (!n_ok || c0 >= cols) continue;
+    __half r[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(v[j] * sx[c0 + j] * swn);
+    if (args.bias != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(__half2float(r[j]) + bn);
+    }
+    __half* yp = args.y + (int64_t)(m0 + c0) * args.N + n;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (c0 + j < cols) yp[(int64_t)j * args.N] = r[j];
+  }
+  epi_sync();  // every thread is past its wait on the counter's first phase
+  if (et == 0) {
+    if (atomicAdd(cnt, 1) == 2 * S - 1) *cnt = 0;  // last of the 2 * splits arrivals
+  }
 }
 
 // Persistent GEMM, data-parallel or stream-K. In stream-K mode the U = tiles *
@@ -224,7 +325,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + C::kStages;
   uint64_t* acc_full = empty + C::kStages;  // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* red_full = acc_empty + 2;       // split-K: partial slices landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_full + 1);
   float* s_sx = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes + C::kBarBytes);  // [2][BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -240,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 128);
     }
+    mbar_init(red_full, 1);
     fence_barrier_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_x) : "memory");
@@ -350,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool owner = kb == 0;
       const bool n_ok = n < args.N;
       float swn = 0.f, bn = 0.f;
-      if (owner) {
+      if (owner || args.splits > 0) {
         // scales are inputs: fetch them while the tile is still accumulating
         for (int j = et; j < cols; j += 128) s_sx[b * BN + j] = args.sx[m0 + j];
         swn = n_ok ? args.sw[n] : 0.f;
@@ -360,6 +463,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t acc = tmem + (uint32_t)(b * C::kAccCols) + ((uint32_t)(q * 32) << 16);
 
+      if (args.splits > 0) {
+        split_epilogue<BN, CH>(args, acc, t, m0, cols, n, n_ok, swn, bn, s_sx + b * BN, my_ws, smem, red_full,
+                               acc_empty + b, et, row);
+        continue;
+      }
       if (!owner) {
         // partial segment: hand the fp32 tile to the owner (column-major: coalesced per warp)
         for (int c0 = 0; c0 < cols; c0 += 16) {
@@ -589,30 +697,48 @@ constexpr size_t kFlagBytes = 1024;  // per-CTA partial-ready flags at the start
 constexpr int kMinUnitsPerCta = 4;
 
 struct Plan {
-  int bn, ch, ctas, dp;
+  int bn, ch, ctas, dp, splits;
 };
 
 // Tile shape and scheduling for an M x N x K problem (rules fitted to B200
 // measurements of the decode and prefill shapes of the Qwen3 family):
-//  * M <= 128: one token tile of BN = M rounded up to 32/64/96/128;
-//    M in (128, 256]: 128-token tiles (two for a 256-sequence decode batch);
-//    M > 256 (prefill): 256-token tiles.
-//  * Whole tiles are dealt round-robin ("data-parallel") when there are at least
-//    half as many tiles as SMs, or when K is short (<= 16 steps) so that a
-//    stream-K fixup would cost more than the idle SMs; otherwise stream-K
-//    splits the tiles x K-steps work evenly over the SMs.
+//  * Decode batches whose weight tiles are fewer than half the SMs (qkv, o and
+//    down projections) when M <= 128, or when K is long (>= 24 steps, the down
+//    projection) for M <= 256: split-K. One token tile of BN = M rounded
+//    up to 32/64/96/128/192/256, `splits` = SMs / weight tiles (<= 8) CTAs per
+//    tile, each streaming 1/splits of K once; the partials are reduced in a
+//    balanced way (each CTA finishes a slice of the tile).
+//  * Other decode shapes (e.g. the gate/up projection): BN = M up to 96, else
+//    128-token tiles; whole tiles dealt round-robin over the SMs.
+//  * M > 256 (prefill): 256-token tiles; whole tiles when they fill the SMs
+//    evenly, else stream-K over tiles x K-steps.
 Plan make_plan(int M, int N, int K, int num_sms) {
-  Plan p{256, (K % kChunk == 0) ? 2 : 1, 1, 0};
+  Plan p{256, (K % kChunk == 0) ? 2 : 1, 1, 0, 0};
+  const int64_t tiles_n = (N + kBM - 1) / kBM;
+  const int64_t steps = (K + kChunk * p.ch - 1) / (kChunk * p.ch);
+  if (M <= 256) {
+    const int full = M <= 32 ? 32 : M <= 64 ? 64 : M <= 96 ? 96 : M <= 128 ? 128 : M <= 192 ? 192 : 256;
+    const int64_t s = num_sms / tiles_n;
+    // For 128 < M <= 256 the 256-token tile's partials (128 KB each) cost more
+    // than they save unless K is long; 128-token tiles dealt whole win there.
+    if (s >= 2 && steps >= 2 && (M <= 128 || steps >= 24)) {
+      p.bn = full;
+      // every K part must hold at least one step: an empty part would hand over an
+      // accumulator the MMA never wrote
+      int64_t sp = s < steps ? s : steps;
+      p.splits = (int)(sp < 8 ? sp : 8);
+      p.ctas = (int)(tiles_n * p.splits);
+      return p;
+    }
+  }
   if (M <= 32) p.bn = 32;
   else if (M <= 64) p.bn = 64;
   else if (M <= 96) p.bn = 96;
   else if (M <= 256) p.bn = 128;
-  const int64_t tiles_n = (N + kBM - 1) / kBM;
   const int64_t tiles_m = (M + p.bn - 1) / p.bn;
   const int64_t T = tiles_n * tiles_m;
-  const int64_t KT = (K + kChunk * p.ch - 1) / (kChunk * p.ch);
   const bool decode = M <= 256 && M > 64;
-  if (decode && (2 * T >= num_sms || KT <= 16)) {
+  if (decode && (2 * T >= num_sms || steps <= 16)) {
     p.dp = 1;
     p.ctas = (int)(T < num_sms ? T : num_sms);
     return p;
@@ -623,7 +749,7 @@ Plan make_plan(int M, int N, int K, int num_sms) {
     p.ctas = num_sms;
     return p;
   }
-  int64_t g = T * KT / kMinUnitsPerCta;
+  int64_t g = T * steps / kMinUnitsPerCta;
   if (g < 1) g = 1;
   if (g > num_sms) g = num_sms;
   if (g > (int64_t)(kFlagBytes / sizeof(int))) g = kFlagBytes / sizeof(int);
@@ -670,6 +796,8 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   args.U = args.T * args.KT;
   args.G = p.ctas;
   args.dp = p.dp;
+  args.splits = p.splits;
+  if (p.splits > args.KT) return cudaErrorInvalidValue;  // a K part without steps
   args.sx = sx;
   args.sw = sw;
   args.bias = (const __half*)bias;

@@ -412,6 +412,11 @@ class ModelRunner:
         torch.cuda.synchronize()
 
     def release_graphs(self) -> None:
-        """Drop the captured graphs (needed before destroying an NCCL process group)."""
+        """Destroy the captured graphs (needed before destroying an NCCL process group:
+        a live graph that holds NCCL calls keeps the communicator busy). reset() frees
+        each executable graph even if a caller still holds a reference to it."""
+        torch.cuda.synchronize(self.device)
+        for g in self.graphs.values():
+            g.reset()
         self.graphs.clear()
         self.graph_pool = None

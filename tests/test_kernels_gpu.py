@@ -102,6 +102,26 @@ def test_fp8_gemm_vs_oracle(M, N, K):
     assert O.rel_l2(y, ref) < 1e-3
 
 
+def test_fp8_gemm_sequence_no_stale_state():
+    """Shapes whose weight tiles are split over several CTAs along K (fewer steps
+    than spare SMs), run back to back with fresh data after other GEMM kernels:
+    every K part must be computed in the current call (tensor memory and the
+    workspace keep values between kernels)."""
+    from microserve_b200 import kernels
+    shapes = [(33, 96, 256), (33, 96, 160), (8, 4096, 512), (33, 128, 160), (64, 96, 160), (33, 96, 288),
+              (256, 4096, 4096), (33, 96, 160), (1, 4096, 4096), (33, 96, 1040)]
+    for i, (M, N, K) in enumerate(shapes):
+        g = torch.Generator().manual_seed(1000 + i)
+        x = torch.randn(M, K, generator=g).half()
+        w = (torch.randn(N, K, generator=g) * 0.02).half()
+        xq, sx = O.quantize_rows(x)
+        wq, sw = O.quantize_weight(w)
+        y = kernels.fp8_gemm(xq.to(DEV), sx.to(DEV), wq.to(DEV), sw.to(DEV)).cpu()
+        ref = O.fp8_gemm(xq, sx, wq, sw)
+        tol = 2e-3 * max(1.0, ref.abs().max().item())
+        assert (y.float() - ref.float()).abs().max().item() <= tol, (M, N, K)
+
+
 def test_fp8_gemm_bias():
     from microserve_b200 import kernels
     torch.manual_seed(3)
