@@ -164,6 +164,18 @@ int ms_paged_prefill_fp8(const void* q, const void* k_cache, const void* v_cache
 int ms_varlen_prefill(const void* q, const void* k, const void* v, const int32_t* cu, void* out, int num_seqs,
                       int64_t total, int Hq, int Hkv, int head_dim, float softmax_scale, void* stream);
 
+/* Greedy token selection: idx[m] = argmax_v x[m, v] over fp16 logits rows
+ * (row stride ldx elements), the first index of the maximum, NaN above every
+ * number, -0.0 equal to +0.0; vmax (may be NULL) receives the maximum as fp32
+ * (for merging vocab-parallel shards). Replaces the greedy branch of `_sample`
+ * (microserve/engine/model_runner.py:33-34, torch.argmax). The workspace
+ * (ms_argmax_workspace_size bytes) must be zeroed before its first use and
+ * used for this entry point only (per-row counters at its start return to zero
+ * after every call). M <= 16384. */
+size_t ms_argmax_workspace_size(int64_t M);
+int ms_argmax_rows(const void* x, int64_t M, int64_t V, int64_t ldx, int64_t* idx, float* vmax, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -24,6 +24,8 @@ SIGNATURES: dict[str, tuple] = {
     "ms_last_error": (C.c_char_p, []),
     "ms_launch_count": (i64, []),
     "ms_set_pdl": (i32, [i32]),
+    "ms_argmax_workspace_size": (sz, [i64]),
+    "ms_argmax_rows": (i32, [vp, i64, i64, i64, vp, vp, vp, sz, vp]),
     "ms_get_device_status": (i32, [C.POINTER(C.c_int), vp]),
     "ms_quantize_rows_fp8": (i32, [vp, i64, i64, i64, vp, vp, vp]),
     "ms_fp8_gemm_workspace_size": (sz, [i64, i64, i64]),

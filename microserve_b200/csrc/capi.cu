@@ -240,4 +240,19 @@ int ms_varlen_prefill(const void* q, const void* k, const void* v, const int32_t
                     "ms_varlen_prefill");
 }
 
+size_t ms_argmax_workspace_size(int64_t M) { return M > 0 ? ms::argmax_workspace_bytes(M) : 0; }
+
+int ms_argmax_rows(const void* x, int64_t M, int64_t V, int64_t ldx, int64_t* idx, float* vmax, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  if (M < 0 || V <= 0 || V > INT32_MAX || ldx < V || M > 16384)
+    return fail(MS_ERR_INVALID, "ms_argmax_rows: bad sizes M=%lld V=%lld ldx=%lld", (long long)M, (long long)V,
+                (long long)ldx);
+  if (M == 0) return MS_OK;
+  if (!x || !idx || !workspace) return fail(MS_ERR_INVALID, "ms_argmax_rows: null pointer");
+  if (workspace_bytes < ms::argmax_workspace_bytes(M))
+    return fail(MS_ERR_WORKSPACE, "ms_argmax_rows: workspace %zu < %zu bytes", workspace_bytes,
+                ms::argmax_workspace_bytes(M));
+  return check_cuda(ms::launch_argmax_rows(x, M, (int)V, ldx, idx, vmax, workspace, S(stream)), "ms_argmax_rows");
+}
+
 }  // extern "C"

@@ -36,6 +36,10 @@ cudaError_t launch_prefill_attention(bool paged, const void* q, const void* k16,
                                      int head_dim, int block_size, int max_blocks, float softmax_scale,
                                      cudaStream_t stream);
 
+size_t argmax_workspace_bytes(int64_t M);
+cudaError_t launch_argmax_rows(const void* x, int64_t M, int V, int64_t ldx, int64_t* idx, float* vmax,
+                               void* workspace, cudaStream_t stream);
+
 void gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* ctas_out);
 size_t gemm_workspace_bytes(int M, int N, int K, int num_sms);
 cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,

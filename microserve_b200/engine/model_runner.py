@@ -295,7 +295,7 @@ class ModelRunner:
     def _logits_and_argmax(self, hidden: torch.Tensor):
         logits = self.model.compute_logits(hidden)
         if tp.tp_size() == 1:
-            return logits, logits.argmax(dim=-1)
+            return logits, kernels.argmax_rows(logits)
         return logits, tp.tp_argmax(logits, self.model.lm_head.vocab_start)
 
     def _sample_rows(self, seqs: list[Sequence], hidden: torch.Tensor) -> list[int | None]:
@@ -351,6 +351,7 @@ class ModelRunner:
                                                                 self.num_kv_heads, max_blocks, self.block_size))
         kernels.workspace.reserve(gemm, self.device, "gemm")
         kernels.workspace.reserve(decode, self.device, "decode")
+        kernels.workspace.reserve(lib.ms_argmax_workspace_size(max_bs), self.device, "argmax")
 
     @torch.inference_mode()
     def _warmup(self) -> None:

@@ -201,3 +201,20 @@ def varlen_prefill(q, k, v, cu, softmax_scale: float) -> torch.Tensor:
     check(_lib.load().ms_varlen_prefill(ptr(q), ptr(k), ptr(v), ptr(cu), ptr(o), cu.shape[0] - 1, T, Hq, Hkv, D,
                                         float(softmax_scale), stream_ptr()), "ms_varlen_prefill")
     return o
+
+
+def argmax_rows(x: torch.Tensor, want_max: bool = False):
+    """Row-wise argmax of fp16 logits [M, V] (unit stride on V): int64 indices
+    (first index of the maximum, NaN highest, torch.argmax's rule) and, if
+    want_max, the fp32 maxima."""
+    _cuda(x, "x")
+    if x.dtype != torch.float16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("argmax_rows: expected fp16 [M, V] with unit stride on V")
+    M, V = x.shape
+    idx = torch.empty(M, dtype=torch.int64, device=x.device)
+    vmax = torch.empty(M, dtype=torch.float32, device=x.device) if want_max else None
+    lib = _lib.load()
+    ws = workspace.get(lib.ms_argmax_workspace_size(M), x.device, "argmax")
+    check(lib.ms_argmax_rows(ptr(x), M, V, x.stride(0), ptr(idx), ptr(vmax), ptr(ws),
+                             0 if ws is None else ws.numel(), stream_ptr()), "ms_argmax_rows")
+    return (idx, vmax) if want_max else idx

@@ -58,7 +58,11 @@ def tp_argmax(local_logits: torch.Tensor, vocab_start: int) -> torch.Tensor:
     """Greedy token over a vocab-parallel logits slice [B, V_local]: the global
     argmax with the smallest index winning ties (torch.argmax's rule), from an
     all-gather of one (max, index) pair per row instead of the logits."""
-    local_max, local_idx = local_logits.float().max(dim=-1)
+    if local_logits.is_cuda and local_logits.dtype == torch.float16:
+        from microserve_b200 import kernels
+        local_idx, local_max = kernels.argmax_rows(local_logits, want_max=True)
+    else:  # host tensors (the gloo tests of this logic)
+        local_max, local_idx = local_logits.float().max(dim=-1)
     if _SIZE == 1:
         return local_idx
     local_idx = local_idx + vocab_start

@@ -375,3 +375,33 @@ def test_varlen_prefill_fresh_kv():
     got = kernels.varlen_prefill(q.cuda(), k.cuda(), v.cuda(), cu.cuda(), D ** -0.5).cpu()
     ref = O.varlen_prefill(q, k, v, cu, D ** -0.5)
     assert (got.float() - ref.float()).abs().max().item() < 0.006
+
+
+# ------------------------------------------------------------------ greedy sampling
+@pytest.mark.parametrize("M,V,pad", [(257, 151936, 0), (3, 1001, 7), (64, 75968, 0)])
+def test_argmax_rows_matches_torch(M, V, pad):
+    """Greedy pick of `_sample` (model_runner.py:33-34): torch.argmax semantics, incl.
+    first index on ties, NaN counted as the maximum and -0.0 == +0.0."""
+    from microserve_b200 import kernels
+    g = torch.Generator().manual_seed(M + V)
+    full = (torch.randn(M, V + pad, generator=g) * 4).half()
+    x = full[:, :V]
+    x[0, 5] = x[0, 900] = 60.0            # tie: first index wins
+    x[1].fill_(-1.0)
+    x[1, 17] = float("nan")               # NaN is the maximum
+    x[2].fill_(-1.0)
+    x[2, 3] = -0.0
+    x[2, 4] = 0.0                         # -0.0 == +0.0: index 3
+    if M > 3:
+        x[3].fill_(float("-inf"))         # all -inf: index 0
+    xd = full.cuda()[:, :V]
+    idx, vmax = kernels.argmax_rows(xd, want_max=True)
+    ref = x.float().argmax(dim=-1)
+    assert torch.equal(idx.cpu(), ref)
+    vm = vmax.cpu()
+    exp = x.float().gather(1, ref[:, None]).squeeze(1)
+    assert torch.equal(torch.isnan(vm), torch.isnan(exp))
+    ok = ~torch.isnan(exp)
+    assert torch.equal(vm[ok], exp[ok])
+    # a second call reuses the (self-resetting) workspace counters
+    assert torch.equal(kernels.argmax_rows(xd).cpu(), ref)
