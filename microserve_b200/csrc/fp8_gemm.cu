@@ -571,6 +571,188 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Wide tiles for decode batches of 129..256 tokens with many weight tiles (the
+// gate/up projection): 256 weight rows x 256 tokens per tile, computed as two
+// M = 128 MMAs that share every activation stage. The activations are read once
+// per 256 weight rows (half the L2 -> SM bytes of 128-row tiles) and a stage is
+// two 32 KB TMA boxes (weights, activations). The two accumulators fill TMEM
+// (512 columns), so a tile's epilogue overlaps only the next tile's loads, not
+// its MMAs. Whole tiles dealt round-robin; 128-byte K steps (2D maps).
+constexpr int kWideRows = 256;
+constexpr int kWideBN = 256;
+constexpr int kWideStages = 3;
+constexpr int kWideABytes = kWideRows * kChunk;                  // 32 KB of weights
+constexpr int kWideStageBytes = kWideABytes + kWideBN * kChunk;  // + 32 KB of activations
+constexpr int kWideBarBytes = 128;
+constexpr int kWideSmem = kWideStages * kWideStageBytes + 1024 + kWideBarBytes + kWideBN * 4;
+constexpr uint32_t kWideIdesc = (1u << 4) | ((uint32_t)(kWideBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+static_assert(kWideSmem <= 227 * 1024, "shared memory budget");
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fp8_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                         GemmArgs args) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];  // aligned by hand, see fp8_gemm_kernel
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kWideStages * kWideStageBytes);
+  uint64_t* empty = full + kWideStages;
+  uint64_t* acc_full = empty + kWideStages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  float* s_sx = reinterpret_cast<float*>(smem + kWideStages * kWideStageBytes + kWideBarBytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = args.KT;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWideStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
+    fence_barrier_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_x) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      int i = 0;
+      bool ok = true, waited = false;
+      for (int64_t t = blockIdx.x; ok && t < args.T; t += args.G) {
+        const int n0 = (int)(t / args.tiles_m) * kWideRows;
+        const int m0 = (int)(t % args.tiles_m) * kWideBN;
+        for (int k = 0; k < KT; ++k, ++i) {
+          const int s = i % kWideStages;
+          if (!mbar_wait(&empty[s], ((uint32_t)(i / kWideStages) & 1u) ^ 1u)) {
+            ok = false;
+            break;
+          }
+          unsigned char* sa = smem + s * kWideStageBytes;
+          mbar_arrive_expect_tx(&full[s], kWideStageBytes);
+          tma_load_2d(&tmap_w, smem_u32(sa), &full[s], k * kChunk, n0);
+          if (!waited) {
+            pdl_wait();
+            waited = true;
+          }
+          tma_load_2d(&tmap_x, smem_u32(sa + kWideABytes), &full[s], k * kChunk, m0);
+        }
+      }
+      pdl_trigger();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      int i = 0, tile = 0;
+      for (int64_t t = blockIdx.x; t < args.T; t += args.G, ++tile) {
+        if (!mbar_wait(acc_empty, ((uint32_t)tile & 1u) ^ 1u)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        bool ok = true;
+        for (int k = 0; k < KT; ++k, ++i) {
+          const int s = i % kWideStages;
+          if (!mbar_wait(&full[s], (uint32_t)(i / kWideStages) & 1u)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = smem_u32(smem + s * kWideStageBytes);
+          const uint32_t b_addr = a_addr + kWideABytes;
+#pragma unroll
+          for (int kk = 0; kk < kChunk / 32; ++kk) {
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+              umma_f8(tmem + (uint32_t)(mt * kWideBN), smem_desc_sw128(a_addr + mt * kBM * kChunk + kk * 32),
+                      smem_desc_sw128(b_addr + kk * 32), kWideIdesc, (k > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(acc_full);
+      }
+    }
+    __syncwarp();
+  } else {  // epilogue: warps 2..5 -> TMEM lane quarters 2, 3, 0, 1
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int et = threadIdx.x - 64;
+    const int64_t N = args.N;
+    pdl_wait();
+    int tile = 0;
+    for (int64_t t = blockIdx.x; t < args.T; t += args.G, ++tile) {
+      const int n0 = (int)(t / args.tiles_m) * kWideRows;
+      const int m0 = (int)(t % args.tiles_m) * kWideBN;
+      const int cols = min(kWideBN, args.M - m0);
+      epi_sync();  // the previous tile's readers of s_sx are done
+      for (int j = et; j < cols; j += 128) s_sx[j] = args.sx[m0 + j];
+      float swn[2], bn[2];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const int n = n0 + mt * kBM + row;
+        swn[mt] = n < N ? args.sw[n] : 0.f;
+        bn[mt] = (n < N && args.bias != nullptr) ? __half2float(args.bias[n]) : 0.f;
+      }
+      if (!mbar_wait(acc_full, (uint32_t)tile & 1u)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      epi_sync();  // s_sx filled
+#pragma unroll 1
+      for (int mt = 0; mt < 2; ++mt) {
+        const int n = n0 + mt * kBM + row;
+        const uint32_t acc = tmem + (uint32_t)(mt * kWideBN) + ((uint32_t)(q * 32) << 16);
+        for (int c0 = 0; c0 < cols; c0 += 16) {
+          float v[16];
+          tmem_ld16(acc + (uint32_t)c0, v);
+          if (n >= N) continue;
+          const float4* sxv = reinterpret_cast<const float4*>(s_sx + c0);
+          float sc[16];
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const float4 f = sxv[g];
+            sc[4 * g] = f.x;
+            sc[4 * g + 1] = f.y;
+            sc[4 * g + 2] = f.z;
+            sc[4 * g + 3] = f.w;
+          }
+          __half r[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(v[j] * sc[j] * swn[mt]);
+          if (args.bias != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(__half2float(r[j]) + bn[mt]);
+          }
+          __half* yp = args.y + (int64_t)(m0 + c0) * N + n;
+          if (c0 + 16 <= cols) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) yp[j * N] = r[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (c0 + j < cols) yp[j * N] = r[j];
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(acc_empty);
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
 // CUDA-core FP8 GEMM for shapes the TMA path cannot describe (K % 16 != 0).
 // One thread per output element; used only for tiny irregular layers.
 __global__ void fp8_gemm_simt_kernel(const uint8_t* __restrict__ xq, const uint8_t* __restrict__ wq, int M, int N,
@@ -697,7 +879,7 @@ constexpr size_t kFlagBytes = 1024;  // per-CTA partial-ready flags at the start
 constexpr int kMinUnitsPerCta = 4;
 
 struct Plan {
-  int bn, ch, ctas, dp, splits;
+  int bn, ch, ctas, dp, splits, wide;
 };
 
 // Tile shape and scheduling for an M x N x K problem (rules fitted to B200
@@ -713,8 +895,17 @@ struct Plan {
 //  * M > 256 (prefill): 256-token tiles; whole tiles when they fill the SMs
 //    evenly, else stream-K over tiles x K-steps.
 Plan make_plan(int M, int N, int K, int num_sms) {
-  Plan p{256, (K % kChunk == 0) ? 2 : 1, 1, 0, 0};
+  Plan p{256, (K % kChunk == 0) ? 2 : 1, 1, 0, 0, 0};
   const int64_t tiles_n = (N + kBM - 1) / kBM;
+  if (M > 128 && M <= 256 && tiles_n > num_sms) {  // e.g. gate/up: 256-row x 256-token tiles
+    const int64_t T = (N + kWideRows - 1) / kWideRows;
+    p.wide = 1;
+    p.dp = 1;
+    p.ch = 1;
+    p.bn = kWideBN;
+    p.ctas = (int)(T < num_sms ? T : num_sms);
+    return p;
+  }
   const int64_t steps = (K + kChunk * p.ch - 1) / (kChunk * p.ch);
   if (M <= 256) {
     const int full = M <= 32 ? 32 : M <= 64 ? 64 : M <= 96 ? 96 : M <= 128 ? 128 : M <= 192 ? 192 : 256;
@@ -785,6 +976,27 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   if (!p.dp && (gemm_workspace_bytes(M, N, K, num_sms) > workspace_bytes || workspace == nullptr))
     return cudaErrorInvalidValue;
   CUtensorMap mw, mx;
+  if (p.wide) {
+    if (!make_map(&mw, wq, N, K, kWideRows, 1) || !make_map(&mx, xq, M, K, kWideBN, 1)) return cudaErrorInvalidValue;
+    GemmArgs args = {};
+    args.M = M;
+    args.N = N;
+    args.K = K;
+    args.KT = (K + kChunk - 1) / kChunk;
+    args.tiles_m = (M + kWideBN - 1) / kWideBN;
+    args.T = (int64_t)((N + kWideRows - 1) / kWideRows) * args.tiles_m;
+    args.U = args.T * args.KT;
+    args.G = p.ctas;
+    args.dp = 1;
+    args.sx = sx;
+    args.sw = sw;
+    args.bias = (const __half*)bias;
+    args.y = (__half*)y;
+    static const cudaError_t attr =
+        cudaFuncSetAttribute(fp8_gemm_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmem);
+    if (attr != cudaSuccess) return attr;
+    return launch_kernel(fp8_gemm_wide_kernel, dim3(args.G), dim3(kThreads), kWideSmem, stream, mw, mx, args);
+  }
   if (!make_map(&mw, wq, N, K, kBM, p.ch) || !make_map(&mx, xq, M, K, bn, p.ch)) return cudaErrorInvalidValue;
   GemmArgs args;
   args.M = M;

@@ -82,6 +82,8 @@ GEMM_SHAPES = [
     (8, 4096, 512), (33, 96, 160),
     # token tiles of 96 / 192 columns, an odd number of 128-byte K chunks, K % 128 != 0
     (96, 4096, 4096), (150, 2048, 4096), (200, 384, 1280), (256, 1024, 1040), (129, 640, 4224),
+    # 256-row x 256-token tiles (129..256 tokens, more 128-row weight tiles than SMs), ragged last tile
+    (256, 24576, 1024), (200, 19000, 512), (129, 24576, 272),
 ]
 
 
@@ -122,12 +124,13 @@ def test_fp8_gemm_sequence_no_stale_state():
         assert (y.float() - ref.float()).abs().max().item() <= tol, (M, N, K)
 
 
-def test_fp8_gemm_bias():
+@pytest.mark.parametrize("M,N,K", [(5, 384, 256), (200, 19000, 256)])
+def test_fp8_gemm_bias(M, N, K):
     from microserve_b200 import kernels
     torch.manual_seed(3)
-    x = torch.randn(5, 256).half()
-    w = (torch.randn(384, 256) * 0.05).half()
-    b = torch.randn(384).half()
+    x = torch.randn(M, K).half()
+    w = (torch.randn(N, K) * 0.05).half()
+    b = torch.randn(N).half()
     xq, sx = O.quantize_rows(x)
     wq, sw = O.quantize_weight(w)
     y = kernels.fp8_gemm(xq.cuda(), sx.cuda(), wq.cuda(), sw.cuda(), b.cuda()).cpu()
