@@ -117,6 +117,7 @@ struct DecodeArgs {
   float* ws_o;                // [B, Hq, S, D]   (S > 1 only)
   float* ws_ml;               // [B, Hq, S, 2]
   int B, Hq, Hkv, block_size, max_blocks, splits;
+  int bs_log2;                // log2(block_size) when it is a power of two, else -1
   float scale_log2;           // softmax_scale * log2(e)
 };
 
@@ -164,23 +165,33 @@ __global__ void __launch_bounds__(kWarps * 32, 3) decode_kernel(DecodeArgs a) {
   // Copy tile number k of this warp (all lanes) into stage k % kStages. The 16
   // tokens of a tile never cross a page (block_size % 16 == 0), and every tile
   // starts below L, so its page is in the table and all 16 rows are in memory.
+  // Per-lane constants of the copies: chunk (r, j) = (q >> 3, q & 7) for q = lane + 32 i,
+  // and the scale row of this lane (k scales in lanes 0-15, v scales in 16-31).
+  uint32_t so[4], go[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int q = lane + 32 * i, r = q >> 3, j = q & 7;
+    so[i] = (uint32_t)(r * 128 + ((j ^ swz(r)) << 4));
+    go[i] = (uint32_t)(r * tok_stride + 16 * j);
+  }
+  const float* sbase = (lane < 16 ? a.k_scale : a.v_scale) + (int64_t)(lane & 15) * a.Hkv + kvh;
+  const uint32_t s_off = (uint32_t)(2 * kTileBytes + (lane >> 4) * 64 + (lane & 15) * 4);
+  const uint8_t* kc = a.k_cache + (int64_t)kvh * kD;
+  const uint8_t* vc = a.v_cache + (int64_t)kvh * kD;
+  const int bs_shift = a.bs_log2;
   auto issue = [&](int k) {
     const int p0 = (first + k * kWarps) << 4;
-    const int page = p0 / a.block_size;
+    const int page = bs_shift >= 0 ? p0 >> bs_shift : p0 / a.block_size;
     const int64_t tok0 = (int64_t)__ldg(bt + page) * a.block_size + (p0 - page * a.block_size);
-    const uint8_t* kb = a.k_cache + (tok0 * a.Hkv + kvh) * kD;
-    const uint8_t* vb = a.v_cache + (tok0 * a.Hkv + kvh) * kD;
+    const uint8_t* kb = kc + tok0 * tok_stride;
+    const uint8_t* vb = vc + tok0 * tok_stride;
     const uint32_t st = wsm_u32 + (uint32_t)((k % kStages) * kStageBytes);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int q = lane + 32 * i, r = q >> 3, j = q & 7;
-      const uint32_t o = (uint32_t)(r * 128 + ((j ^ swz(r)) << 4));
-      cp_async16(st + o, kb + r * tok_stride + 16 * j);
-      cp_async16(st + kTileBytes + o, vb + r * tok_stride + 16 * j);
+      cp_async16(st + so[i], kb + go[i]);
+      cp_async16(st + kTileBytes + so[i], vb + go[i]);
     }
-    const int r = lane & 15;
-    const float* sp = (lane < 16 ? a.k_scale : a.v_scale) + (tok0 + r) * a.Hkv + kvh;
-    cp_async4(st + 2 * kTileBytes + (lane >> 4) * 64 + r * 4, sp);
+    cp_async4(st + s_off, sbase + tok0 * a.Hkv);
   };
 #pragma unroll
   for (int k = 0; k < kStages; ++k) {
@@ -420,6 +431,7 @@ cudaError_t launch_decode_attention(const void* q, const void* k_cache, const vo
   a.Hq = Hq;
   a.Hkv = Hkv;
   a.block_size = block_size;
+  a.bs_log2 = (block_size & (block_size - 1)) == 0 ? __builtin_ctz((unsigned)block_size) : -1;
   a.max_blocks = max_blocks;
   a.splits = splits;
   a.scale_log2 = softmax_scale * kLog2e;
