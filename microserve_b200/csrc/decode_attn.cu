@@ -27,8 +27,9 @@
 //    activation quantisation downstream turns fp16-level attention errors
 //    into visible output differences. P' changes from the accumulator layout
 //    to the operand layout with movmatrix (an in-register 8x8 transpose).
-//  * Online softmax in the exp2 domain; warps of a CTA interleave 16-token
-//    tiles and are merged through shared memory at the end. Long contexts with
+//  * Online softmax in the exp2 domain, one running-max update per pair of
+//    16-token tiles; warps of a CTA interleave tiles and are merged through
+//    shared memory at the end. Long contexts with
 //    few sequences are split over CTAs (flash-decoding); partial (m, l, o)
 //    rows go to a workspace and a second kernel merges them.
 #include <mutex>
@@ -199,92 +200,39 @@ __global__ void __launch_bounds__(kWarps * 32, 3) decode_kernel(DecodeArgs a) {
     cp_async_commit();  // one group per tile slot, empty or not
   }
 
-  for (int k = 0; k < n_my; ++k) {
-    cp_async_wait<kStages - 1>();  // this lane's copies of tile k have landed
-    __syncwarp();                  // ... and every other lane's
-    const int p0 = (first + k * kWarps) << 4;
-    const unsigned char* sk = wsm + (k % kStages) * kStageBytes;
-    const unsigned char* sv = sk + kTileBytes;
-    const float* sks = reinterpret_cast<const float*>(sk + 2 * kTileBytes);
-    auto ld = [](const unsigned char* t, int r, int j) {
-      return *reinterpret_cast<const uint4*>(t + r * 128 + ((j ^ swz(r)) << 4));
-    };
-    // K rows g, g+8: chunks c and 4 + c
-    const uint4 k0a = ld(sk, g, c), k0b = ld(sk, g, 4 + c);
+  auto ld = [](const unsigned char* t, int r, int j) {
+    return *reinterpret_cast<const uint4*>(t + r * 128 + ((j ^ swz(r)) << 4));
+  };
+  // S^T = K . Q^T for the tile in ring slot `slot`: s[0], s[1] = token g, heads 2c, 2c+1;
+  // s[2], s[3] = token g + 8 (raw dot products, before the k scale).
+  auto scores = [&](int slot, float (&sc)[4]) {
+    const unsigned char* sk = wsm + slot * kStageBytes;
+    const uint4 k0a = ld(sk, g, c), k0b = ld(sk, g, 4 + c);  // K rows g, g+8: chunks c and 4 + c
     const uint4 k1a = ld(sk, g + 8, c), k1b = ld(sk, g + 8, 4 + c);
-    // V rows 2c, 2c+1, 2c+8, 2c+9: chunk g
-    uint4 v0 = ld(sv, 2 * c, g), v1 = ld(sv, 2 * c + 1, g);
+    const uint32_t kw0[8] = {k0a.x, k0a.y, k0a.z, k0a.w, k0b.x, k0b.y, k0b.z, k0b.w};
+    const uint32_t kw1[8] = {k1a.x, k1a.y, k1a.z, k1a.w, k1b.x, k1b.y, k1b.z, k1b.w};
+    sc[0] = sc[1] = sc[2] = sc[3] = 0.f;
+#pragma unroll
+    for (int st = 0; st < 8; ++st) {
+      const int j = st >> 2, w = st & 3;
+      const uint32_t r0 = e4m3x2_to_f16x2((uint16_t)(kw0[st] & 0xffff));
+      const uint32_t r2 = e4m3x2_to_f16x2((uint16_t)(kw0[st] >> 16));
+      const uint32_t r1 = e4m3x2_to_f16x2((uint16_t)(kw1[st] & 0xffff));
+      const uint32_t r3 = e4m3x2_to_f16x2((uint16_t)(kw1[st] >> 16));
+      mma16816(sc, r0, r1, r2, r3, qf[j][2 * w], qf[j][2 * w + 1]);
+    }
+  };
+  // O^T += V^T . P'^T for the tile in ring slot `slot`, V rows past the end zeroed.
+  auto accumulate = [&](int slot, int p0, uint32_t pb0, uint32_t pb1, uint32_t pc0, uint32_t pc1) {
+    const unsigned char* sv = wsm + slot * kStageBytes + kTileBytes;
+    uint4 v0 = ld(sv, 2 * c, g), v1 = ld(sv, 2 * c + 1, g);  // V rows 2c, 2c+1, 2c+8, 2c+9: chunk g
     uint4 v2 = ld(sv, 2 * c + 8, g), v3 = ld(sv, 2 * c + 9, g);
-    const float ks0 = sks[g], ks1 = sks[g + 8];
-    const float vs0 = sks[16 + g], vs1 = sks[16 + g + 8];
-    __syncwarp();  // every lane has its fragments: the stage may be refilled
-    if (k + kStages < n_my) issue(k + kStages);
-    cp_async_commit();
-    const bool tail = p0 + 16 > L;
-    if (tail) {  // zero V rows past the end so stale bytes can never reach the product
+    if (p0 + 16 > L) {  // stale bytes past the end can never reach the product
       if (p0 + 2 * c >= L) v0 = make_uint4(0, 0, 0, 0);
       if (p0 + 2 * c + 1 >= L) v1 = make_uint4(0, 0, 0, 0);
       if (p0 + 2 * c + 8 >= L) v2 = make_uint4(0, 0, 0, 0);
       if (p0 + 2 * c + 9 >= L) v3 = make_uint4(0, 0, 0, 0);
     }
-
-    // ---- S^T = K . Q^T -------------------------------------------------
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
-    {
-      const uint32_t kw0[8] = {k0a.x, k0a.y, k0a.z, k0a.w, k0b.x, k0b.y, k0b.z, k0b.w};
-      const uint32_t kw1[8] = {k1a.x, k1a.y, k1a.z, k1a.w, k1b.x, k1b.y, k1b.z, k1b.w};
-#pragma unroll
-      for (int st = 0; st < 8; ++st) {
-        const int j = st >> 2, w = st & 3;
-        const uint32_t r0 = e4m3x2_to_f16x2((uint16_t)(kw0[st] & 0xffff));
-        const uint32_t r2 = e4m3x2_to_f16x2((uint16_t)(kw0[st] >> 16));
-        const uint32_t r1 = e4m3x2_to_f16x2((uint16_t)(kw1[st] & 0xffff));
-        const uint32_t r3 = e4m3x2_to_f16x2((uint16_t)(kw1[st] >> 16));
-        mma16816(s, r0, r1, r2, r3, qf[j][2 * w], qf[j][2 * w + 1]);
-      }
-    }
-    // s[0], s[1]: token g, heads 2c, 2c+1; s[2], s[3]: token g+8.
-    const bool ok0 = p0 + g < L, ok1 = p0 + g + 8 < L;
-    s[0] = ok0 ? s[0] * ks0 * a.scale_log2 : -INFINITY;
-    s[1] = ok0 ? s[1] * ks0 * a.scale_log2 : -INFINITY;
-    s[2] = ok1 ? s[2] * ks1 * a.scale_log2 : -INFINITY;
-    s[3] = ok1 ? s[3] * ks1 * a.scale_log2 : -INFINITY;
-
-    // Fold the per-token v scale into the exponent: w = p * v_scale = exp2(s + log2(v_scale) - m),
-    // with the running max m taken over s + log2(v_scale), so every weight is in (0, 1] and its
-    // f16 hi/lo split (below) keeps ~22 bits. The denominator sums exp2(s - m) in fp32.
-    const float lv0 = ok0 ? lg2(vs0) : 0.f, lv1 = ok1 ? lg2(vs1) : 0.f;
-    const float w0 = s[0] + lv0, w1 = s[1] + lv0, w2 = s[2] + lv1, w3 = s[3] + lv1;
-    float tmax0 = fmaxf(w0, w2), tmax1 = fmaxf(w1, w3);
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      tmax0 = fmaxf(tmax0, __shfl_xor_sync(0xffffffffu, tmax0, o));
-      tmax1 = fmaxf(tmax1, __shfl_xor_sync(0xffffffffu, tmax1, o));
-    }
-    const float mn0 = fmaxf(m_run[0], tmax0), mn1 = fmaxf(m_run[1], tmax1);
-    // The first tile always holds token p0 < L, so mn is finite here.
-    const float al0 = ex2(m_run[0] - mn0), al1 = ex2(m_run[1] - mn1);
-    m_run[0] = mn0;
-    m_run[1] = mn1;
-    l_run[0] = l_run[0] * al0 + ex2(s[0] - mn0) + ex2(s[2] - mn0);
-    l_run[1] = l_run[1] * al1 + ex2(s[1] - mn1) + ex2(s[3] - mn1);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      acc[i][0] *= al0; acc[i][1] *= al1;
-      acc[i][2] *= al0; acc[i][3] *= al1;
-    }
-    // P'^T operand, as f16 hi + lo parts, transposed to the B layout. The weights are
-    // scaled by 2^kPScaleLog2 (undone in the final division) so that lo stays a normal
-    // f16 for every weight that matters (P' >= 2^-16).
-    const float q00 = ex2(w0 - mn0 + kPScaleLog2), q01 = ex2(w1 - mn1 + kPScaleLog2);
-    const float q10 = ex2(w2 - mn0 + kPScaleLog2), q11 = ex2(w3 - mn1 + kPScaleLog2);
-    const uint32_t h0 = pack_h2(q00, q01), h1 = pack_h2(q10, q11);
-    const float2 h0f = h2_to_f2(h0), h1f = h2_to_f2(h1);
-    const uint32_t l0 = pack_h2(q00 - h0f.x, q01 - h0f.y), l1 = pack_h2(q10 - h1f.x, q11 - h1f.y);
-    const uint32_t pb0 = movmatrix_trans(h0), pb1 = movmatrix_trans(h1);
-    const uint32_t pc0 = movmatrix_trans(l0), pc1 = movmatrix_trans(l1);
-
-    // ---- O^T += V^T . P'^T ---------------------------------------------
     const uint32_t va[4] = {v0.x, v0.y, v0.z, v0.w};
     const uint32_t vb[4] = {v1.x, v1.y, v1.z, v1.w};
     const uint32_t vc[4] = {v2.x, v2.y, v2.z, v2.w};
@@ -303,6 +251,85 @@ __global__ void __launch_bounds__(kWarps * 32, 3) decode_kernel(DecodeArgs a) {
       mma16816(acc[i], a0, a1, a2, a3, pb0, pb1);
       mma16816(acc[i], a0, a1, a2, a3, pc0, pc1);
     }
+  };
+
+  // Two tiles (k, k + 1) per iteration: one running-max update, one rescale of
+  // the accumulators and one set of shuffles serve 32 tokens.
+  for (int k = 0; k < n_my; k += 2) {
+    cp_async_wait<kStages - 2>();  // this lane's copies of tiles k, k + 1 have landed
+    __syncwarp();                  // ... and every other lane's
+    const bool has1 = k + 1 < n_my;
+    const int slot0 = k % kStages, slot1 = (k + 1) % kStages;
+    const int pa = (first + k * kWarps) << 4, pb = (first + (k + 1) * kWarps) << 4;
+    float sA[4], sB[4];
+    scores(slot0, sA);
+    if (has1) scores(slot1, sB);
+    const float* ksA = reinterpret_cast<const float*>(wsm + slot0 * kStageBytes + 2 * kTileBytes);
+    const float* ksB = reinterpret_cast<const float*>(wsm + slot1 * kStageBytes + 2 * kTileBytes);
+    // token validity; the second tile counts as empty when this warp has no tile k + 1
+    const bool a0 = pa + g < L, a1 = pa + g + 8 < L;
+    const bool b0 = has1 && pb + g < L, b1 = has1 && pb + g + 8 < L;
+    sA[0] = a0 ? sA[0] * ksA[g] * a.scale_log2 : -INFINITY;
+    sA[1] = a0 ? sA[1] * ksA[g] * a.scale_log2 : -INFINITY;
+    sA[2] = a1 ? sA[2] * ksA[g + 8] * a.scale_log2 : -INFINITY;
+    sA[3] = a1 ? sA[3] * ksA[g + 8] * a.scale_log2 : -INFINITY;
+    sB[0] = b0 ? sB[0] * ksB[g] * a.scale_log2 : -INFINITY;
+    sB[1] = b0 ? sB[1] * ksB[g] * a.scale_log2 : -INFINITY;
+    sB[2] = b1 ? sB[2] * ksB[g + 8] * a.scale_log2 : -INFINITY;
+    sB[3] = b1 ? sB[3] * ksB[g + 8] * a.scale_log2 : -INFINITY;
+
+    // Fold the per-token v scale into the exponent: w = p * v_scale = exp2(s + log2(v_scale) - m),
+    // with the running max m taken over s + log2(v_scale), so every weight is in (0, 1] and its
+    // f16 hi/lo split (below) keeps ~22 bits. The denominator sums exp2(s - m) in fp32.
+    const float lvA0 = a0 ? lg2(ksA[16 + g]) : 0.f, lvA1 = a1 ? lg2(ksA[16 + g + 8]) : 0.f;
+    const float lvB0 = b0 ? lg2(ksB[16 + g]) : 0.f, lvB1 = b1 ? lg2(ksB[16 + g + 8]) : 0.f;
+    const float wA[4] = {sA[0] + lvA0, sA[1] + lvA0, sA[2] + lvA1, sA[3] + lvA1};
+    const float wB[4] = {sB[0] + lvB0, sB[1] + lvB0, sB[2] + lvB1, sB[3] + lvB1};
+    float tmax0 = fmaxf(fmaxf(wA[0], wA[2]), fmaxf(wB[0], wB[2]));
+    float tmax1 = fmaxf(fmaxf(wA[1], wA[3]), fmaxf(wB[1], wB[3]));
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      tmax0 = fmaxf(tmax0, __shfl_xor_sync(0xffffffffu, tmax0, o));
+      tmax1 = fmaxf(tmax1, __shfl_xor_sync(0xffffffffu, tmax1, o));
+    }
+    const float mn0 = fmaxf(m_run[0], tmax0), mn1 = fmaxf(m_run[1], tmax1);
+    // Tile k always holds token pa < L, so mn is finite here.
+    const float al0 = ex2(m_run[0] - mn0), al1 = ex2(m_run[1] - mn1);
+    m_run[0] = mn0;
+    m_run[1] = mn1;
+    l_run[0] = l_run[0] * al0 + ((ex2(sA[0] - mn0) + ex2(sA[2] - mn0)) + (ex2(sB[0] - mn0) + ex2(sB[2] - mn0)));
+    l_run[1] = l_run[1] * al1 + ((ex2(sA[1] - mn1) + ex2(sA[3] - mn1)) + (ex2(sB[1] - mn1) + ex2(sB[3] - mn1)));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      acc[i][0] *= al0; acc[i][1] *= al1;
+      acc[i][2] *= al0; acc[i][3] *= al1;
+    }
+    // P'^T operands, as f16 hi + lo parts, transposed to the B layout. The weights are
+    // scaled by 2^kPScaleLog2 (undone in the final division) so that lo stays a normal
+    // f16 for every weight that matters (P' >= 2^-16).
+    auto pmat = [&](const float (&w)[4], uint32_t& pb0, uint32_t& pb1, uint32_t& pc0, uint32_t& pc1) {
+      const float q00 = ex2(w[0] - mn0 + kPScaleLog2), q01 = ex2(w[1] - mn1 + kPScaleLog2);
+      const float q10 = ex2(w[2] - mn0 + kPScaleLog2), q11 = ex2(w[3] - mn1 + kPScaleLog2);
+      const uint32_t h0 = pack_h2(q00, q01), h1 = pack_h2(q10, q11);
+      const float2 h0f = h2_to_f2(h0), h1f = h2_to_f2(h1);
+      const uint32_t l0 = pack_h2(q00 - h0f.x, q01 - h0f.y), l1 = pack_h2(q10 - h1f.x, q11 - h1f.y);
+      pb0 = movmatrix_trans(h0);
+      pb1 = movmatrix_trans(h1);
+      pc0 = movmatrix_trans(l0);
+      pc1 = movmatrix_trans(l1);
+    };
+    uint32_t pb0, pb1, pc0, pc1;
+    pmat(wA, pb0, pb1, pc0, pc1);
+    accumulate(slot0, pa, pb0, pb1, pc0, pc1);
+    if (has1) {
+      pmat(wB, pb0, pb1, pc0, pc1);
+      accumulate(slot1, pb, pb0, pb1, pc0, pc1);
+    }
+    __syncwarp();  // every lane is done with both slots: they may be refilled
+    if (k + kStages < n_my) issue(k + kStages);
+    cp_async_commit();
+    if (k + 1 + kStages < n_my) issue(k + 1 + kStages);
+    cp_async_commit();
   }
 
   // ---- merge warps ---------------------------------------------------------
