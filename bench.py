@@ -162,7 +162,8 @@ def build_engine(args, cfg, max_model_len):
                             kv_cache_dtype="fp8_e4m3", max_num_seqs=args.batch,
                             max_num_batched_tokens=args.max_batched_tokens, max_model_len=max_model_len,
                             tensor_parallel_size=args.gpus, gpu_memory_utilization=0.9, seed=0,
-                            num_kvcache_blocks=args.kv_blocks))
+                            num_kvcache_blocks=args.kv_blocks,
+                            tp_fused_collective=not getattr(args, "nccl_allreduce", False)))
 
 
 def sync_all():
@@ -478,6 +479,8 @@ def run_ours(args):
                    "model": f"qwen3-{args.model}", "global_batch": B, "seq_len": int(batch["ctx0"].mean()),
                    "parallelism": f"tp{args.gpus}", "kv_cache": "fp8_e4m3, 256-token pages",
                    "pdl": not args.no_pdl,
+                   "tp_collective": ("nccl all-reduce" if args.nccl_allreduce else
+                                     "fused peer-memory all-reduce+rmsnorm+fp8") if args.gpus > 1 else None,
                    "l2": "inputs larger than L2 (weights + KV >> 126 MB); no flush"},
         "roofline": dict(roof, peak_kind=f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s"),
@@ -667,6 +670,8 @@ def main():
     ap.add_argument("--max-batched-tokens", type=int, default=8192)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nccl-allreduce", action="store_true",
+                    help="tensor parallel: NCCL all-reduce instead of the fused peer-memory kernel")
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch the library's kernels without programmatic dependent launch")
     ap.add_argument("--kv-blocks", type=int, default=0, help="KV-cache blocks (0: size from free memory)")

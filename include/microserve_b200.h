@@ -176,6 +176,34 @@ size_t ms_argmax_workspace_size(int64_t M);
 int ms_argmax_rows(const void* x, int64_t M, int64_t V, int64_t ldx, int64_t* idx, float* vmax, void* workspace,
                    size_t workspace_bytes, void* stream);
 
+/* ---- tensor parallel over NVLink peer memory (no reference counterpart for the
+ * plumbing; the fused op replaces dist.all_reduce + add/RMSNorm + act quant) ----
+ *
+ * ms_ipc_handle: CUDA IPC handle (64 bytes) of the allocation holding `ptr` and
+ * ptr's offset inside it; ms_ipc_open maps a peer's handle in this process
+ * (base to close later, ptr = base + offset); ms_ipc_close unmaps. */
+int ms_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+int ms_ipc_open(const void* handle, int64_t offset, void** base_out, void** ptr_out);
+int ms_ipc_close(void* base);
+
+/* Row-parallel all-reduce + residual add + RMSNorm + FP8 row quantisation, one
+ * kernel per rank. partial[p], gather_q[p], gather_s[p], gather_h[p] (optional)
+ * and flags[p] are rank p's buffers as mapped in this process: partial = rank p's
+ * row-parallel output [M, H] fp16; gather_q/gather_s = [M, H] e4m3 / [M] fp32
+ * that receive every rank's rows; gather_h = [M, H] fp16 rows (the final norm);
+ * flags = [2 * world] int32, zero before the first call. ctrl: this rank's
+ * [2] int32 (zero before the first call). Rank r reduces and normalises rows
+ * [r * R, (r + 1) * R), R = ceil(M / world), updating those rows of its residual
+ * [M, H] in place, and writes them to every rank; the kernel returns after every
+ * rank's rows are in this rank's gather buffers. Replaces RowParallelLinear's
+ * dist.all_reduce (microserve/layers/linear.py:70-77) + the add/RMSNorm that
+ * follows (layers/layernorm.py:22-42) + the next FP8 activation quantisation
+ * (layers/fp8_linear.py:14-23). world <= 8, H % 8 == 0, H <= 16384. */
+int ms_tp_allreduce_rmsnorm_fp8(const void* const* partial, void* const* gather_q, float* const* gather_s,
+                                void* const* gather_h, int* const* flags, int* ctrl, void* residual,
+                                const void* weight, int rank, int world, int64_t M, int64_t H, float eps,
+                                void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -2,6 +2,10 @@
 (microserve/Config.py:4-38) plus
   tensor_parallel_size - GPUs per model replica (one process per GPU, group
                          set up by the launcher, see utils/dist.py);
+  tp_fused_collective  - with tensor parallelism on the FP8 path, sum the
+                         row-parallel outputs with this library's peer-memory
+                         kernel fused with add + RMSNorm + FP8 quantisation
+                         (utils/tp_fused.py) instead of NCCL all-reduce;
   load_format          - "safetensors" (model_dir holds the checkpoint) or
                          "dummy" (seeded N(0, 0.02) random weights of the
                          shape in model_dir/config.json or `hf_config`);
@@ -35,6 +39,7 @@ class Config:
     kv_cache_dtype: str = "fp8_e4m3"
     scheduler_policy: str = "mixed"
     tensor_parallel_size: int = 1
+    tp_fused_collective: bool = True
     load_format: str = "safetensors"
     hf_config: object = None
 

@@ -25,6 +25,10 @@ SIGNATURES: dict[str, tuple] = {
     "ms_launch_count": (i64, []),
     "ms_set_pdl": (i32, [i32]),
     "ms_argmax_workspace_size": (sz, [i64]),
+    "ms_ipc_handle": (i32, [vp, vp, C.POINTER(C.c_int64)]),
+    "ms_ipc_open": (i32, [vp, i64, C.POINTER(vp), C.POINTER(vp)]),
+    "ms_ipc_close": (i32, [vp]),
+    "ms_tp_allreduce_rmsnorm_fp8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i64, i64, f32, vp]),
     "ms_argmax_rows": (i32, [vp, i64, i64, i64, vp, vp, vp, sz, vp]),
     "ms_get_device_status": (i32, [C.POINTER(C.c_int), vp]),
     "ms_quantize_rows_fp8": (i32, [vp, i64, i64, i64, vp, vp, vp]),

@@ -7,6 +7,8 @@
 #include <string>
 
 #include "../../include/microserve_b200.h"
+#include <cstring>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -253,6 +255,67 @@ int ms_argmax_rows(const void* x, int64_t M, int64_t V, int64_t ldx, int64_t* id
     return fail(MS_ERR_WORKSPACE, "ms_argmax_rows: workspace %zu < %zu bytes", workspace_bytes,
                 ms::argmax_workspace_bytes(M));
   return check_cuda(ms::launch_argmax_rows(x, M, (int)V, ldx, idx, vmax, workspace, S(stream)), "ms_argmax_rows");
+}
+
+// --------------------------------------------------------------------------- tensor parallel
+int ms_ipc_handle(const void* ptr, void* handle, int64_t* offset) {
+  if (!ptr || !handle || !offset) return fail(MS_ERR_INVALID, "ms_ipc_handle: null pointer");
+  // the allocation that holds ptr (driver entry point: the library does not link libcuda)
+  typedef CUresult (*RangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static RangeFn range_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range_fn = reinterpret_cast<RangeFn>(f);
+  });
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn == nullptr || range_fn(&base, &size, (CUdeviceptr)ptr) != CUDA_SUCCESS)
+    return fail(MS_ERR_CUDA, "ms_ipc_handle: cuMemGetAddressRange failed");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, (void*)base);
+  if (e != cudaSuccess) return check_cuda(e, "ms_ipc_handle");
+  memcpy(handle, &h, sizeof(h));
+  *offset = (int64_t)((CUdeviceptr)ptr - base);
+  return MS_OK;
+}
+
+int ms_ipc_open(const void* handle, int64_t offset, void** base_out, void** ptr_out) {
+  if (!handle || !base_out || !ptr_out || offset < 0) return fail(MS_ERR_INVALID, "ms_ipc_open: bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return check_cuda(e, "ms_ipc_open");
+  *base_out = base;
+  *ptr_out = (char*)base + offset;
+  return MS_OK;
+}
+
+int ms_ipc_close(void* base) {
+  if (!base) return fail(MS_ERR_INVALID, "ms_ipc_close: null pointer");
+  return check_cuda(cudaIpcCloseMemHandle(base), "ms_ipc_close");
+}
+
+int ms_tp_allreduce_rmsnorm_fp8(const void* const* partial, void* const* gather_q, float* const* gather_s,
+                                void* const* gather_h, int* const* flags, int* ctrl, void* residual,
+                                const void* weight, int rank, int world, int64_t M, int64_t H, float eps,
+                                void* stream) {
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || M < 0 || M > INT32_MAX || H <= 0 || H % 8 != 0 ||
+      H > 16384)
+    return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: bad sizes rank=%d world=%d M=%lld H=%lld", rank,
+                world, (long long)M, (long long)H);
+  if (!partial || !gather_q || !gather_s || !flags || !ctrl || !residual || !weight)
+    return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: null pointer");
+  for (int p = 0; p < world; ++p)
+    if (!partial[p] || !gather_q[p] || !gather_s[p] || !flags[p] || (gather_h && !gather_h[p]))
+      return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: null peer pointer (rank %d)", p);
+  return check_cuda(ms::launch_tp_allreduce_rmsnorm_fp8(partial, gather_q, gather_s, gather_h, flags, ctrl, residual,
+                                                        weight, rank, world, (int)M, (int)H, eps, S(stream)),
+                    "ms_tp_allreduce_rmsnorm_fp8");
 }
 
 }  // extern "C"

@@ -36,6 +36,11 @@ cudaError_t launch_prefill_attention(bool paged, const void* q, const void* k16,
                                      int head_dim, int block_size, int max_blocks, float softmax_scale,
                                      cudaStream_t stream);
 
+cudaError_t launch_tp_allreduce_rmsnorm_fp8(const void* const* partial, void* const* gather_q,
+                                            float* const* gather_s, void* const* gather_h, int* const* flags,
+                                            int* ctrl, void* residual, const void* weight, int rank, int world,
+                                            int M, int H, float eps, cudaStream_t stream);
+
 size_t argmax_workspace_bytes(int64_t M);
 cudaError_t launch_argmax_rows(const void* x, int64_t M, int V, int64_t ldx, int64_t* idx, float* vmax,
                                void* workspace, cudaStream_t stream);

@@ -113,6 +113,15 @@ class ModelRunner:
             if config.dtype != torch.float16:
                 raise ValueError("FP8 quantization requires torch.float16")
             self.num_quantized_linears = quantize_fp8_linears(self.model)
+        # Tensor parallel on the FP8 path: row-parallel sums fused with the add + RMSNorm +
+        # FP8 quantisation that follow them, over peer memory (utils/tp_fused.py).
+        self.tp_fused = None
+        if (tp.tp_size() > 1 and config.tp_fused_collective and self.num_quantized_linears > 0
+                and config.kv_cache_dtype == "fp8_e4m3"):
+            from microserve_b200.utils.tp_fused import TpFused
+            rows = max(config.max_num_batched_tokens, (config.max_num_seqs + 15) // 16 * 16)
+            self.tp_fused = TpFused(rows, hf.hidden_size, self.device)
+            self.model.model.tp_fused = self.tp_fused
         torch.cuda.empty_cache()
 
         if self.num_blocks <= 0:

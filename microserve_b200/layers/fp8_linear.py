@@ -57,9 +57,12 @@ class FP8DynamicLinear(nn.Module):
             return None
         return self.bias
 
-    def forward_fp8(self, xq: torch.Tensor, sx: torch.Tensor, reduce: bool = True) -> torch.Tensor:
-        """GEMM on an already-quantised activation (fused producers)."""
-        y = kernels.fp8_gemm(xq, sx, self.weight_fp8, self.weight_scale, self._bias_here())
+    def forward_fp8(self, xq: torch.Tensor, sx: torch.Tensor, reduce: bool = True,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+        """GEMM on an already-quantised activation (fused producers). A row-parallel
+        layer sums its output over the group unless reduce=False (the fused
+        tensor-parallel op then reads the partial from `out`)."""
+        y = kernels.fp8_gemm(xq, sx, self.weight_fp8, self.weight_scale, self._bias_here(), out=out)
         if reduce and self.tp_mode == "row":
             tp.all_reduce_(y)
         return y

@@ -73,8 +73,10 @@ class Qwen3Attention(nn.Module):
         o = self.attn(q, k, v)
         return self.o_proj(o.reshape(-1, self.num_heads * self.head_dim))
 
-    def forward_fp8(self, positions: torch.Tensor, xq: torch.Tensor, sx: torch.Tensor) -> torch.Tensor:
-        """Fused FP8 path; xq/sx are the FP8 rows of the normed hidden states."""
+    def forward_fp8(self, positions: torch.Tensor, xq: torch.Tensor, sx: torch.Tensor,
+                    partial_out: torch.Tensor | None = None) -> torch.Tensor:
+        """Fused FP8 path; xq/sx are the FP8 rows of the normed hidden states. With
+        partial_out the row-parallel o_proj writes its unreduced output there."""
         ctx = get_context()
         attn = self.attn
         qkv = self.qkv_proj.forward_fp8(xq, sx)
@@ -86,7 +88,7 @@ class Qwen3Attention(nn.Module):
             (attn.k_cache, attn.v_cache, attn.k_scale_cache, attn.v_scale_cache), want_kv=want_kv)
         o = attn.forward_cached(q, k, v)
         oq, so = kernels.quantize_rows_fp8(o.view(-1, self.q_size))
-        return self.o_proj.forward_fp8(oq, so)
+        return self.o_proj.forward_fp8(oq, so, reduce=partial_out is None, out=partial_out)
 
 
 class Qwen3MLP(nn.Module):
@@ -100,10 +102,11 @@ class Qwen3MLP(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return self.down_proj(self.act_fn(self.gate_up_proj(x)))
 
-    def forward_fp8(self, xq: torch.Tensor, sx: torch.Tensor) -> torch.Tensor:
+    def forward_fp8(self, xq: torch.Tensor, sx: torch.Tensor, partial_out: torch.Tensor | None = None
+                    ) -> torch.Tensor:
         gu = self.gate_up_proj.forward_fp8(xq, sx)
         aq, sa = self.act_fn.forward_fp8(gu)
-        return self.down_proj.forward_fp8(aq, sa)
+        return self.down_proj.forward_fp8(aq, sa, reduce=partial_out is None, out=partial_out)
 
 
 class Qwen3DecoderLayer(nn.Module):
@@ -138,15 +141,27 @@ class Qwen3DecoderLayer(nn.Module):
         return hidden_states, residual
 
     def forward_fp8(self, positions: torch.Tensor, hidden_states: torch.Tensor,
-                    residual: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor]:
+                    residual: torch.Tensor | None, tpf=None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Fused FP8 layer. With tpf (utils.tp_fused.TpFused, tensor parallel) the
+        row-parallel outputs stay unreduced in the peer buffer and each sum + add +
+        RMSNorm + FP8 quantisation is one kernel; hidden_states is then the previous
+        layer's partial output and the residual is current on this rank's rows."""
+        rows = hidden_states.shape[0]
         if residual is None:
             xq, sx, _ = self.input_layernorm.forward_fp8(hidden_states)
             residual = hidden_states
+        elif tpf is not None:
+            xq, sx = tpf.allreduce_norm_fp8(rows, residual, self.input_layernorm.weight, self.input_layernorm.eps, 0)
         else:
             xq, sx, residual = self.input_layernorm.forward_fp8(hidden_states, residual)
-        h = self.self_attn.forward_fp8(positions, xq, sx)
-        xq, sx, residual = self.post_attention_layernorm.forward_fp8(h, residual)
-        return self.mlp.forward_fp8(xq, sx), residual
+        part = tpf.partial(rows) if tpf is not None else None
+        h = self.self_attn.forward_fp8(positions, xq, sx, partial_out=part)
+        if tpf is not None:
+            xq, sx = tpf.allreduce_norm_fp8(rows, residual, self.post_attention_layernorm.weight,
+                                            self.post_attention_layernorm.eps, 1)
+        else:
+            xq, sx, residual = self.post_attention_layernorm.forward_fp8(h, residual)
+        return self.mlp.forward_fp8(xq, sx, partial_out=part), residual
 
 
 class Qwen3Model(nn.Module):
@@ -164,11 +179,14 @@ class Qwen3Model(nn.Module):
         hidden_states = self.embed_tokens(input_ids)
         residual = None
         fused = self._fp8_ready()
+        tpf = getattr(self, "tp_fused", None) if fused else None
         for layer in self.layers:
             if fused:
-                hidden_states, residual = layer.forward_fp8(positions, hidden_states, residual)
+                hidden_states, residual = layer.forward_fp8(positions, hidden_states, residual, tpf)
             else:
                 hidden_states, residual = layer(positions, hidden_states, residual)
+        if tpf is not None:
+            return tpf.allreduce_norm_fp16(hidden_states.shape[0], residual, self.norm.weight, self.norm.eps)
         return self.norm(hidden_states, residual)[0]
 
 
