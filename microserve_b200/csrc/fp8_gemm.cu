@@ -911,8 +911,10 @@ Plan make_plan(int M, int N, int K, int num_sms) {
     const int full = M <= 32 ? 32 : M <= 64 ? 64 : M <= 96 ? 96 : M <= 128 ? 128 : M <= 192 ? 192 : 256;
     const int64_t s = num_sms / tiles_n;
     // For 128 < M <= 256 the 256-token tile's partials (128 KB each) cost more
-    // than they save unless K is long; 128-token tiles dealt whole win there.
-    if (s >= 2 && steps >= 2 && (M <= 128 || steps >= 24)) {
+    // than they save unless K is long or 128-token tiles dealt whole would leave
+    // three quarters of the SMs idle (the small shards of tensor parallelism).
+    const int64_t dp_tiles = tiles_n * ((M + kBM - 1) / kBM);
+    if (s >= 2 && steps >= 2 && (M <= 128 || steps >= 24 || 4 * dp_tiles < num_sms)) {
       p.bn = full;
       // every K part must hold at least one step: an empty part would hand over an
       // accumulator the MMA never wrote

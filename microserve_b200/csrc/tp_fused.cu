@@ -95,10 +95,15 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_fp8_kernel(TpAr
   __syncthreads();
   const int e = s_e;
   if (blockIdx.x < a.rows) row_work(a, a.row0 + blockIdx.x, red);
-  // done: the last block publishes this rank's rows and waits for everyone's
-  __threadfence_system();
+  // done: the last block publishes this rank's rows and waits for everyone's. One
+  // system-scope fence per block, after the block barrier, orders every thread's
+  // peer stores before the arrival (the fence is cumulative); a fence in every
+  // thread would serialise thousands of system-scope fences.
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(a.ctrl + 1, 1) == (int)gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    s_last = atomicAdd(a.ctrl + 1, 1) == (int)gridDim.x - 1;
+  }
   __syncthreads();
   if (threadIdx.x == 0 && s_last) {
     __threadfence_system();
@@ -120,21 +125,27 @@ __device__ __forceinline__ void row_work(const TpArgs& a, int64_t m, float* red)
   for (int i = 0; i < kMaxVec; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
-  for (int p = 0; p < a.world; ++p) {
-    const H8* src = reinterpret_cast<const H8*>(a.partial[p] + base);
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = threadIdx.x + i * kThreads;
-      if (c < nv) {
-        // L1 bypassed: the same addresses were read one op earlier with other contents
-        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src) + c);
-        H8 x;
-        memcpy(&x, &u, sizeof(x));
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kThreads;
+    if (c < nv) {
+      // every rank's vector in flight before any add (one round trip over NVLink);
+      // L1 bypassed: the same addresses were read one op earlier with other contents
+      uint4 u[kMaxWorld];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __half22float2(x.h[j]);
-          v[i][2 * j] += f.x;
-          v[i][2 * j + 1] += f.y;
+      for (int p = 0; p < kMaxWorld; ++p)
+        if (p < a.world) u[p] = __ldcg(reinterpret_cast<const uint4*>(a.partial[p] + base) + c);
+#pragma unroll
+      for (int p = 0; p < kMaxWorld; ++p) {
+        if (p < a.world) {
+          H8 x;
+          memcpy(&x, &u[p], sizeof(x));
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(x.h[j]);
+            v[i][2 * j] += f.x;
+            v[i][2 * j + 1] += f.y;
+          }
         }
       }
     }

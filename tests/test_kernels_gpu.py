@@ -84,6 +84,8 @@ GEMM_SHAPES = [
     (96, 4096, 4096), (150, 2048, 4096), (200, 384, 1280), (256, 1024, 1040), (129, 640, 4224),
     # 256-row x 256-token tiles (129..256 tokens, more 128-row weight tiles than SMs), ragged last tile
     (256, 24576, 1024), (200, 19000, 512), (129, 24576, 272),
+    # tensor-parallel shards: few weight tiles at 256 tokens (split-K)
+    (256, 768, 4096), (256, 4096, 512),
 ]
 
 
