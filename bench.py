@@ -281,7 +281,8 @@ def time_kernel(fn, iters=20, warm=3):
 
 @torch.inference_mode()
 def kernel_rooflines(engine, batch, step_idx, hbm_peak):
-    """Per-kernel achieved HBM bandwidth on the decode step's own inputs (layer 0)."""
+    """Per-kernel achieved HBM bandwidth on the decode step's own inputs: attention over
+    layer 0's KV cache (larger than L2), each GEMM cycling through the layers' weights."""
     from microserve_b200 import kernels
     runner = engine.runner
     model = runner.model
@@ -299,13 +300,23 @@ def kernel_rooflines(engine, batch, step_idx, hbm_peak):
     ctx = lens.double().sum().item()
     attn_bytes = ctx * Hkv * (2 * HEAD_DIM + 2 * 4) + 2 * B * Hq * HEAD_DIM * 2 + B * (4 + 4 * batch["bt"].shape[1])
     res = {"decode_attention": dict(seconds=t_attn, bytes=attn_bytes, per_layer=1)}
-    lins = {"qkv_proj": layer.self_attn.qkv_proj, "o_proj": layer.self_attn.o_proj,
-            "gate_up_proj": layer.mlp.gate_up_proj, "down_proj": layer.mlp.down_proj}
-    for name, lin in lins.items():
+    layers = model.model.layers
+    lins = {"qkv_proj": [l.self_attn.qkv_proj for l in layers], "o_proj": [l.self_attn.o_proj for l in layers],
+            "gate_up_proj": [l.mlp.gate_up_proj for l in layers], "down_proj": [l.mlp.down_proj for l in layers]}
+    for name, per_layer in lins.items():
+        lin = per_layer[0]
         x = torch.randn(B, lin.in_features, device=dev, dtype=torch.float16)
         xq, sx = kernels.quantize_rows_fp8(x)
         y = torch.empty(B, lin.out_features, device=dev, dtype=torch.float16)
-        t = time_kernel(lambda: kernels.fp8_gemm(xq, sx, lin.weight_fp8, lin.weight_scale, out=y))
+        it = [0]
+
+        def launch():
+            # consecutive launches use consecutive layers' weights, as in the decode step,
+            # so the weights come from HBM and not from L2
+            w = per_layer[it[0] % len(per_layer)]
+            kernels.fp8_gemm(xq, sx, w.weight_fp8, w.weight_scale, out=y)
+            it[0] += 1
+        t = time_kernel(launch)
         byts = lin.out_features * lin.in_features + B * lin.in_features + 2 * B * lin.out_features \
             + 4 * (B + lin.out_features)
         res[name] = dict(seconds=t, bytes=byts, per_layer=1)

@@ -56,6 +56,7 @@ struct GemmArgs {
   __half* y;
   float* ws;   // [G][BN][kBM] fp32 partial tiles (stream-K fixup)
   int* flags;  // [G] partial-ready flags; zero before and after every launch
+  int tma_y;   // 1: the output tensor map is valid (N % 8 == 0, y 16-byte aligned)
 };
 
 // BN: token columns per tile (MMA N). CH: 128-byte K chunks per pipeline stage.
@@ -109,6 +110,58 @@ __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint32_t dst
           "r"(dst),
       "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Bulk tensor store of a staged output tile (shared -> global), then wait until
+// it is complete. One thread.
+__device__ __forceinline__ void tma_store_2d_wait(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(c0),
+               "r"(c1), "r"(src)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Output of 16 token columns of one weight row n: y = fp16(fp16(v * sx * sw[n]) + bias[n]).
+// With `stage` the values go to a shared-memory tile [tokens][128 rows] fp16 (the
+// CTA then writes the tile with one bulk tensor store); without, straight to y
+// with one 2-byte store per token (64 bytes per warp instruction, which keeps a
+// tile's epilogue several microseconds long when it cannot overlap a main loop).
+__device__ __forceinline__ void out16(const GemmArgs& args, const float* v, const float* sx, float swn, float bn,
+                                      int m0, int c0, int cols, int n, __half* stage, int row) {
+  const float4* sxv = reinterpret_cast<const float4*>(sx + c0);
+  float sc[16];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const float4 f = sxv[g];
+    sc[4 * g] = f.x;
+    sc[4 * g + 1] = f.y;
+    sc[4 * g + 2] = f.z;
+    sc[4 * g + 3] = f.w;
+  }
+  __half r[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(v[j] * sc[j] * swn);
+  if (args.bias != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(__half2float(r[j]) + bn);
+  }
+  if (stage != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) stage[(c0 + j) * kBM + row] = r[j];
+    return;
+  }
+  if (n >= args.N) return;
+  const int64_t N = args.N;
+  __half* yp = args.y + (int64_t)(m0 + c0) * N + n;
+  if (c0 + 16 <= cols) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) yp[j * N] = r[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (c0 + j < cols) yp[j * N] = r[j];
+  }
 }
 
 // One stage of an operand: CH chunks starting at K step k, rows from `row`.
@@ -312,8 +365,9 @@ __device__ __forceinline__ void split_epilogue(const GemmArgs& args, uint32_t ac
 template <int BN, int CH>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                    GemmArgs args) {
+                    const __grid_constant__ CUtensorMap tmap_y, GemmArgs args) {
   using C = Cfg<BN, CH>;
+  static_assert(C::kStages * C::kStageBytes >= BN * kBM * 2, "staged output tile fits the stages");
   // The 128B swizzle atoms need 1024-byte alignment. The dynamic window is only
   // guaranteed 16-byte aligned (it follows any static shared memory), so align by
   // hand; declaring the array __align__(1024) would let the compiler fold the
@@ -437,8 +491,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;  // row within the 128-row weight tile
     const int et = threadIdx.x - 64;
     float* my_ws = args.ws + (int64_t)cta * BN * kBM;
-    __half* __restrict__ y = args.y;
-    const int64_t N = args.N;
     pdl_wait();  // token scales come from the preceding grid; the workspace may be in use until it ends
     int seg = -1;
     SegIter it(args, cta);
@@ -501,6 +553,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      // The CTA's last segment: its loads have landed and its MMAs are done, so the
+      // stage buffers are free to hold the output tile for one bulk tensor store.
+      __half* stage = nullptr;
+      if (args.tma_y) {
+        SegIter rest = it;
+        int64_t t2;
+        int kb2, ke2;
+        if (!rest.next(t2, kb2, ke2)) stage = reinterpret_cast<__half*>(smem);
+      }
       epi_sync();  // s_sx filled; contributors' partials visible
       for (int c0 = 0; c0 < cols; c0 += 16) {
         float v[16];
@@ -524,34 +585,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (!n_ok) continue;
-        // all 16 results in registers first, then the stores back to back
-        const float4* sxv = reinterpret_cast<const float4*>(s_sx + b * BN + c0);
-        float sc[16];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const float4 f = sxv[g];
-          sc[4 * g] = f.x;
-          sc[4 * g + 1] = f.y;
-          sc[4 * g + 2] = f.z;
-          sc[4 * g + 3] = f.w;
-        }
-        __half r[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(v[j] * sc[j] * swn);
-        if (args.bias != nullptr) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(__half2float(r[j]) + bn);
-        }
-        __half* yp = y + (int64_t)(m0 + c0) * N + n;
-        if (c0 + 16 <= cols) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) yp[j * N] = r[j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (c0 + j < cols) yp[j * N] = r[j];
-        }
+        out16(args, v, s_sx + b * BN, swn, bn, m0, c0, cols, n, stage, row);
+      }
+      if (stage != nullptr) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staged tile -> the bulk store
+        epi_sync();
+        if (et == 0) tma_store_2d_wait(&tmap_y, smem_u32(stage), (int)(t / args.tiles_m) * kBM, m0);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&acc_empty[b]);
@@ -587,10 +626,11 @@ constexpr int kWideBarBytes = 128;
 constexpr int kWideSmem = kWideStages * kWideStageBytes + 1024 + kWideBarBytes + kWideBN * 4;
 constexpr uint32_t kWideIdesc = (1u << 4) | ((uint32_t)(kWideBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 static_assert(kWideSmem <= 227 * 1024, "shared memory budget");
+static_assert(2 * kWideBN * kBM * 2 <= kWideStages * kWideStageBytes, "staged output tile fits the stages");
 
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                         GemmArgs args) {
+                         const __grid_constant__ CUtensorMap tmap_y, GemmArgs args) {
   extern __shared__ __align__(16) unsigned char smem_raw[];  // aligned by hand, see fp8_gemm_kernel
   const uint32_t raw_addr = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
@@ -703,41 +743,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!mbar_wait(acc_full, (uint32_t)tile & 1u)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      // The CTA's last tile: every load has landed and every MMA is done, so the
+      // stage buffers hold the two 128-row halves of the output tile ([256 tokens]
+      // [128 rows] fp16 each) for two bulk tensor stores.
+      const bool staged = args.tma_y && t + args.G >= args.T;
       epi_sync();  // s_sx filled
 #pragma unroll 1
       for (int mt = 0; mt < 2; ++mt) {
         const int n = n0 + mt * kBM + row;
         const uint32_t acc = tmem + (uint32_t)(mt * kWideBN) + ((uint32_t)(q * 32) << 16);
+        __half* stage = staged ? reinterpret_cast<__half*>(smem + (size_t)mt * kWideBN * kBM * 2) : nullptr;
         for (int c0 = 0; c0 < cols; c0 += 16) {
           float v[16];
           tmem_ld16(acc + (uint32_t)c0, v);
-          if (n >= N) continue;
-          const float4* sxv = reinterpret_cast<const float4*>(s_sx + c0);
-          float sc[16];
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const float4 f = sxv[g];
-            sc[4 * g] = f.x;
-            sc[4 * g + 1] = f.y;
-            sc[4 * g + 2] = f.z;
-            sc[4 * g + 3] = f.w;
-          }
-          __half r[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(v[j] * sc[j] * swn[mt]);
-          if (args.bias != nullptr) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(__half2float(r[j]) + bn[mt]);
-          }
-          __half* yp = args.y + (int64_t)(m0 + c0) * N + n;
-          if (c0 + 16 <= cols) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) yp[j * N] = r[j];
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (c0 + j < cols) yp[j * N] = r[j];
-          }
+          out16(args, v, s_sx, swn[mt], bn[mt], m0, c0, cols, n, stage, row);
+        }
+      }
+      if (staged) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staged tile -> the bulk stores
+        epi_sync();
+        if (et == 0) {
+          for (int mt = 0; mt < 2; ++mt)
+            if (n0 + mt * kBM < N)
+              tma_store_2d_wait(&tmap_y, smem_u32(smem + (size_t)mt * kWideBN * kBM * 2), n0 + mt * kBM, m0);
         }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -827,7 +855,16 @@ bool make_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int
   EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr) return false;
   CUresult r;
-  if (ch == 1) {
+  if (ch == 0) {
+    // fp16 output y [rows = tokens, cols = N], box = [box_rows tokens][128 weight rows], no swizzle
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBM, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    r = enc(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else if (ch == 1) {
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)cols};
     cuuint32_t box[2] = {(cuuint32_t)kChunk, (cuuint32_t)box_rows};
@@ -853,7 +890,8 @@ bool make_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int
 }
 
 template <int BN, int CH>
-cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& args, cudaStream_t stream) {
+cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs& args,
+                      cudaStream_t stream) {
   using C = Cfg<BN, CH>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -866,13 +904,14 @@ cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const GemmAr
   // (one per SM) must become resident. The preceding grid never waits on this
   // one, so its SMs free up; the next grid cannot start before every CTA here
   // has triggered (after issuing its last load), i.e. before all are resident.
-  return launch_kernel(fp8_gemm_kernel<BN, CH>, dim3(args.G), dim3(kThreads), C::kSmemBytes, stream, mw, mx, args);
+  return launch_kernel(fp8_gemm_kernel<BN, CH>, dim3(args.G), dim3(kThreads), C::kSmemBytes, stream, mw, mx, my,
+                       args);
 }
 
 template <int BN>
-cudaError_t launch_bn(int ch, const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& args,
-                      cudaStream_t stream) {
-  return ch == 2 ? launch_tc<BN, 2>(mw, mx, args, stream) : launch_tc<BN, 1>(mw, mx, args, stream);
+cudaError_t launch_bn(int ch, const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& my,
+                      const GemmArgs& args, cudaStream_t stream) {
+  return ch == 2 ? launch_tc<BN, 2>(mw, mx, my, args, stream) : launch_tc<BN, 1>(mw, mx, my, args, stream);
 }
 
 constexpr size_t kFlagBytes = 1024;  // per-CTA partial-ready flags at the start of the workspace
@@ -890,8 +929,13 @@ struct Plan {
 //    up to 32/64/96/128/192/256, `splits` = SMs / weight tiles (<= 8) CTAs per
 //    tile, each streaming 1/splits of K once; the partials are reduced in a
 //    balanced way (each CTA finishes a slice of the tile).
-//  * Other decode shapes (e.g. the gate/up projection): BN = M up to 96, else
-//    128-token tiles; whole tiles dealt round-robin over the SMs.
+//  * 129..256 tokens with more 128-row weight tiles than SMs (the gate/up
+//    projection): 256 x 256 tiles of fp8_gemm_wide_kernel, dealt whole.
+//  * Other decode shapes: BN = M up to 96, else 128-token tiles; whole tiles
+//    dealt round-robin over the SMs.
+// Every CTA writes its last output tile through shared memory with a bulk
+// tensor store when N % 8 == 0 (earlier tiles' epilogues overlap the next main
+// loop and keep direct stores).
 //  * M > 256 (prefill): 256-token tiles; whole tiles when they fill the SMs
 //    evenly, else stream-K over tiles x K-steps.
 Plan make_plan(int M, int N, int K, int num_sms) {
@@ -977,7 +1021,10 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   const int bn = p.bn;
   if (!p.dp && (gemm_workspace_bytes(M, N, K, num_sms) > workspace_bytes || workspace == nullptr))
     return cudaErrorInvalidValue;
-  CUtensorMap mw, mx;
+  CUtensorMap mw, mx, my;
+  // The bulk store of a CTA's last output tile needs 16-byte aligned rows of y.
+  const bool tma_y = N % 8 == 0 && ((uintptr_t)y & 15) == 0 && make_map(&my, y, M, N, bn, 0);
+  if (!tma_y) memset(&my, 0, sizeof(my));
   if (p.wide) {
     if (!make_map(&mw, wq, N, K, kWideRows, 1) || !make_map(&mx, xq, M, K, kWideBN, 1)) return cudaErrorInvalidValue;
     GemmArgs args = {};
@@ -990,6 +1037,7 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
     args.U = args.T * args.KT;
     args.G = p.ctas;
     args.dp = 1;
+    args.tma_y = tma_y ? 1 : 0;
     args.sx = sx;
     args.sw = sw;
     args.bias = (const __half*)bias;
@@ -997,7 +1045,7 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
     static const cudaError_t attr =
         cudaFuncSetAttribute(fp8_gemm_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmem);
     if (attr != cudaSuccess) return attr;
-    return launch_kernel(fp8_gemm_wide_kernel, dim3(args.G), dim3(kThreads), kWideSmem, stream, mw, mx, args);
+    return launch_kernel(fp8_gemm_wide_kernel, dim3(args.G), dim3(kThreads), kWideSmem, stream, mw, mx, my, args);
   }
   if (!make_map(&mw, wq, N, K, kBM, p.ch) || !make_map(&mx, xq, M, K, bn, p.ch)) return cudaErrorInvalidValue;
   GemmArgs args;
@@ -1011,6 +1059,7 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   args.G = p.ctas;
   args.dp = p.dp;
   args.splits = p.splits;
+  args.tma_y = tma_y ? 1 : 0;
   if (p.splits > args.KT) return cudaErrorInvalidValue;  // a K part without steps
   args.sx = sx;
   args.sw = sw;
@@ -1019,12 +1068,12 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   args.flags = p.dp ? nullptr : (int*)workspace;
   args.ws = p.dp ? nullptr : (float*)((char*)workspace + kFlagBytes);
   switch (bn) {
-    case 32: return launch_bn<32>(p.ch, mw, mx, args, stream);
-    case 64: return launch_bn<64>(p.ch, mw, mx, args, stream);
-    case 96: return launch_bn<96>(p.ch, mw, mx, args, stream);
-    case 128: return launch_bn<128>(p.ch, mw, mx, args, stream);
-    case 192: return launch_bn<192>(p.ch, mw, mx, args, stream);
-    default: return launch_bn<256>(p.ch, mw, mx, args, stream);
+    case 32: return launch_bn<32>(p.ch, mw, mx, my, args, stream);
+    case 64: return launch_bn<64>(p.ch, mw, mx, my, args, stream);
+    case 96: return launch_bn<96>(p.ch, mw, mx, my, args, stream);
+    case 128: return launch_bn<128>(p.ch, mw, mx, my, args, stream);
+    case 192: return launch_bn<192>(p.ch, mw, mx, my, args, stream);
+    default: return launch_bn<256>(p.ch, mw, mx, my, args, stream);
   }
 }
 

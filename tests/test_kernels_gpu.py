@@ -82,10 +82,13 @@ GEMM_SHAPES = [
     (8, 4096, 512), (33, 96, 160),
     # token tiles of 96 / 192 columns, an odd number of 128-byte K chunks, K % 128 != 0
     (96, 4096, 4096), (150, 2048, 4096), (200, 384, 1280), (256, 1024, 1040), (129, 640, 4224),
-    # 256-row x 256-token tiles (129..256 tokens, more 128-row weight tiles than SMs), ragged last tile
-    (256, 24576, 1024), (200, 19000, 512), (129, 24576, 272),
+    # 256-row x 256-token tiles (129..256 tokens, more 128-row weight tiles than SMs), ragged last tile;
+    # the 8B gate/up projection first; (160, 40000, 640) deals two tiles to some CTAs
+    (256, 24576, 4096), (256, 24576, 1024), (200, 19000, 512), (160, 40000, 640), (129, 24576, 272),
     # tensor-parallel shards: few weight tiles at 256 tokens (split-K)
     (256, 768, 4096), (256, 4096, 512),
+    # N % 8 != 0: rows of y not 16-byte aligned, so the last tile is stored directly (no bulk store)
+    (64, 1001, 512), (256, 6150, 1024), (200, 19001, 512), (700, 1003, 1024),
 ]
 
 
@@ -113,7 +116,8 @@ def test_fp8_gemm_sequence_no_stale_state():
     workspace keep values between kernels)."""
     from microserve_b200 import kernels
     shapes = [(33, 96, 256), (33, 96, 160), (8, 4096, 512), (33, 128, 160), (64, 96, 160), (33, 96, 288),
-              (256, 4096, 4096), (33, 96, 160), (1, 4096, 4096), (33, 96, 1040)]
+              (256, 4096, 4096), (33, 96, 160), (256, 24576, 1024), (1, 4096, 4096), (200, 19000, 512),
+              (33, 96, 1040)]
     for i, (M, N, K) in enumerate(shapes):
         g = torch.Generator().manual_seed(1000 + i)
         x = torch.randn(M, K, generator=g).half()
@@ -126,7 +130,7 @@ def test_fp8_gemm_sequence_no_stale_state():
         assert (y.float() - ref.float()).abs().max().item() <= tol, (M, N, K)
 
 
-@pytest.mark.parametrize("M,N,K", [(5, 384, 256), (200, 19000, 256)])
+@pytest.mark.parametrize("M,N,K", [(5, 384, 256), (200, 19000, 256), (200, 19000, 512)])
 def test_fp8_gemm_bias(M, N, K):
     from microserve_b200 import kernels
     torch.manual_seed(3)
