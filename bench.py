@@ -600,13 +600,36 @@ def run_reference(args):
 
 
 @torch.inference_mode()
+def reference_kernels():
+    """The reference's own GPU kernels (Triton), from its offline install in baseline/_ref:
+    (fp8_decode_attention, _fp8_mm), or None when that install is absent."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "microserve")):
+        return None
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    from microserve.layers.fp8_decode_attention import fp8_decode_attention
+    from microserve.layers.fp8_linear import _fp8_mm
+    return fp8_decode_attention, _fp8_mm
+
+
 def run_kernel(args):
     """One kernel on synthetic inputs of a Qwen3 layer's shapes, timed with CUDA events
     (used for the kernel sweeps of BASELINE config 5 and for ncu captures). One JSON line
-    per case."""
+    per case. With --impl reference the reference's own Triton kernel runs on the same
+    inputs (decode attention: fp8_decode_attention; GEMM: _fp8_mm on pre-quantised
+    activations, as ms_fp8_gemm takes them), the GPU "beat this" bar."""
     from microserve_b200 import _lib, kernels
     from oracle import fp8_decoder as O
-    _lib.load()
+    ref = None
+    if args.impl == "reference":
+        ref = reference_kernels()
+        if ref is None:
+            print(json.dumps({"impl": "reference", "kernel": args.kernel,
+                              "unavailable": "reference not installed in baseline/_ref"}), flush=True)
+            return
+    else:
+        _lib.load()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     m = MODELS[args.model]
@@ -629,10 +652,15 @@ def run_kernel(args):
             lens = torch.full((B,), ctx, dtype=torch.int32, device=dev)
             q = torch.randn(B, Hq, HEAD_DIM, device=dev, dtype=torch.float16, generator=g)
             out = torch.empty_like(q)
-            t = time_kernel(lambda: kernels.paged_decode_fp8(q, kc, vc, ks, vs, lens, bt, HEAD_DIM ** -0.5, out=out),
-                            iters=args.steps, warm=args.warmup)
+            if ref is not None:
+                t = time_kernel(lambda: ref[0](q, kc, vc, ks, vs, lens, bt, HEAD_DIM ** -0.5),
+                                iters=args.steps, warm=args.warmup)
+            else:
+                t = time_kernel(lambda: kernels.paged_decode_fp8(q, kc, vc, ks, vs, lens, bt, HEAD_DIM ** -0.5,
+                                                                 out=out), iters=args.steps, warm=args.warmup)
             byts = B * ctx * Hkv * (2 * HEAD_DIM + 8) + 2 * B * Hq * HEAD_DIM * 2 + B * (4 + 4 * nb)
-            print(json.dumps({"kernel": "decode_attention", "model": args.model, "tp": args.gpus, "batch": B,
+            print(json.dumps({"kernel": "decode_attention", "impl": args.impl, "model": args.model, "tp": args.gpus,
+                              "batch": B,
                               "ctx": ctx, "q_heads": Hq, "kv_heads": Hkv, "us": round(t * 1e6, 2),
                               "bytes": byts, "GBps": round(byts / t / 1e9, 1),
                               "frac_hbm": round(byts / t / 1e9 / hbm_peak, 4)}), flush=True)
@@ -657,12 +685,16 @@ def run_kernel(args):
             it = [0]
 
             def launch():
-                kernels.fp8_gemm(xq, sx, wqs[it[0] % copies], sw, out=y)
+                if ref is not None:  # the reference's grid (fp8_linear.py:75-77)
+                    ref[1][((M + 15) // 16, (N + 63) // 64)](xq, wqs[it[0] % copies], sx, sw, y, M, N, K)
+                else:
+                    kernels.fp8_gemm(xq, sx, wqs[it[0] % copies], sw, out=y)
                 it[0] += 1
             t = time_kernel(launch, iters=args.steps, warm=args.warmup)
             byts = N * K + M * K + 2 * M * N + 4 * (M + N)
             flops = 2 * M * N * K
-            print(json.dumps({"kernel": "fp8_gemm", "M": M, "N": N, "K": K, "us": round(t * 1e6, 2),
+            print(json.dumps({"kernel": "fp8_gemm", "impl": args.impl, "M": M, "N": N, "K": K,
+                              "us": round(t * 1e6, 2),
                               "GBps": round(byts / t / 1e9, 1), "frac_hbm": round(byts / t / 1e9 / hbm_peak, 4),
                               "TFLOPs": round(flops / t / 1e12, 1)}), flush=True)
 
@@ -693,10 +725,10 @@ def main():
                     help="--kernel gemm: M:N:K comma list (default: the 8B layer's four linears at M=--batch)")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
-    if args.impl == "reference":
+    if args.kernel is not None:
+        run_kernel(args)  # --impl reference: the reference's own Triton kernel on the same inputs
+    elif args.impl == "reference":
         run_reference(args)
-    elif args.kernel is not None:
-        run_kernel(args)
     else:
         run_ours(args)
 
