@@ -320,6 +320,30 @@ def kernel_rooflines(engine, batch, step_idx, hbm_peak):
         byts = lin.out_features * lin.in_features + B * lin.in_features + 2 * B * lin.out_features \
             + 4 * (B + lin.out_features)
         res[name] = dict(seconds=t, bytes=byts, per_layer=1)
+    # the row kernels between them, on the step's own shapes (inputs in L2, as in the step)
+    H, I = layer.mlp.down_proj.out_features, layer.mlp.down_proj.in_features
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(B, H, device=dev, generator=g).half()
+    r = torch.randn(B, H, device=dev, generator=g).half()
+    nw = layer.post_attention_layernorm.weight
+    eps = layer.post_attention_layernorm.eps
+    t = time_kernel(lambda: kernels.rmsnorm(x, nw, eps, r, want_fp16=False, want_fp8=True))
+    res["rmsnorm_fp8"] = dict(seconds=t, bytes=B * H * 7 + 4 * B + 2 * H, per_layer=2)
+    gu = torch.randn(B, 2 * I, device=dev, generator=g).half()
+    t = time_kernel(lambda: kernels.silu_mul(gu, want_fp16=False, want_fp8=True))
+    res["silu_mul_fp8"] = dict(seconds=t, bytes=B * 2 * I * 2 + B * I + 4 * B, per_layer=1)
+    sa = layer.self_attn
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * HEAD_DIM, device=dev, generator=g).half()
+    pos, slots = batch["pos"][step_idx], batch["slots"][step_idx]
+    t = time_kernel(lambda: kernels.qkv_post(
+        qkv, Hq, Hkv, HEAD_DIM, pos, sa.rotary_emb.cos_half16, sa.rotary_emb.sin_half16, sa.q_norm.weight,
+        sa.k_norm.weight, sa.rms_norm_eps, slots, (attn.k_cache, attn.v_cache, attn.k_scale_cache,
+                                                   attn.v_scale_cache)))
+    res["qkv_post"] = dict(seconds=t, bytes=B * (Hq + 2 * Hkv) * HEAD_DIM * 2 + B * Hq * HEAD_DIM * 2
+                           + B * Hkv * (2 * HEAD_DIM + 8), per_layer=1)
+    o = torch.randn(B, Hq * HEAD_DIM, device=dev, generator=g).half()
+    t = time_kernel(lambda: kernels.quantize_rows_fp8(o))
+    res["quantize_rows"] = dict(seconds=t, bytes=B * Hq * HEAD_DIM * 3 + 4 * B, per_layer=1)
     for v in res.values():
         v["achieved_gbs"] = v["bytes"] / v["seconds"] / 1e9
         v["frac"] = v["achieved_gbs"] / hbm_peak

@@ -100,6 +100,22 @@ __device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float a, float b) {
   return (uint16_t)r;
 }
 
+// x / s rounded to nearest (the IEEE quotient) from r = RN(1/s), in five
+// flops instead of a full-precision divide: q0 = RN(x r) is within ~1.5 ulp of
+// x/s; one correction q1 = RN(q0 + r RN(x - s q0)) brings it within half an ulp
+// plus a negligible term, i.e. faithful; a second correction from the faithful
+// q1 is correctly rounded by Markstein's theorem (with r within half an ulp of
+// 1/s the remainder x - s q1 is exact under FMA and RN(q1 + r (x - s q1)) =
+// RN(x/s)). Needs no underflow in the remainder: holds for the FP8 encoders
+// here (fp16 x, s >= 1e-8 / 448, |x/s| <= 448). Zeros are returned as they are:
+// the corrections would turn -0 into +0 (-0 + +0 = +0), and -0 / s is -0.
+__device__ __forceinline__ float div_by_rcp(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float q1 = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
+  const float q2 = __fmaf_rn(__fmaf_rn(-q1, s, x), r, q1);
+  return x == 0.f ? x : q2;
+}
+
 __device__ __forceinline__ uint8_t f32_to_e4m3(float a) {
   a = fminf(fmaxf(a, -MS_FP8_MAX), MS_FP8_MAX);
   return (uint8_t)__nv_cvt_float_to_fp8(a, __NV_SATFINITE, __NV_E4M3);

@@ -35,6 +35,7 @@ def test_quantize_rows_bit_exact(shape):
     torch.manual_seed(0)
     x = torch.randn(shape, dtype=torch.float16) * 3
     x[0].zero_()  # all-zero row -> scale 1e-8 / 448
+    x[-1, ::7] = -0.0  # negative zeros encode as 0x80
     q, s = kernels.quantize_rows_fp8(x.to(DEV))
     qr, sr = O.quantize_rows(x)
     assert torch.equal(s.cpu(), sr)
