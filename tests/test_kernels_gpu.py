@@ -88,6 +88,8 @@ GEMM_SHAPES = [
     (256, 24576, 4096), (256, 24576, 1024), (200, 19000, 512), (160, 40000, 640), (129, 24576, 272),
     # tensor-parallel shards: few weight tiles at 256 tokens (split-K)
     (256, 768, 4096), (256, 4096, 512),
+    # 129..256 tokens dealt as 64- / 96-token tiles (o and qkv projections at 256 tokens, a ragged last tile)
+    (256, 4096, 4096), (160, 4096, 2048),
     # N % 8 != 0: rows of y not 16-byte aligned, so the last tile is stored directly (no bulk store)
     (64, 1001, 512), (256, 6150, 1024), (200, 19001, 512), (700, 1003, 1024),
 ]
