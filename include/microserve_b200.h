@@ -78,7 +78,7 @@ size_t ms_fp8_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 int ms_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias, void* y,
                 int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
 
-/* RMSNorm over rows of H (H % 16 == 0), optionally fused with the residual
+/* RMSNorm over rows of H (H % 16 == 0, H <= 32768), optionally fused with the residual
  * add and an FP8 quantisation of the output:
  *   residual == NULL: y = fp16(fp16(x * rsqrt(mean(x^2) + eps)) * weight)
  *   residual != NULL: r = fp16(x + residual) -> residual_out; y = norm(r)
@@ -88,7 +88,7 @@ int ms_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw
 int ms_rmsnorm(const void* x, const void* residual, const void* weight, int64_t M, int64_t H, float eps,
                void* residual_out, void* y, void* yq, float* sy, void* stream);
 
-/* SiLU-and-mul over gu [M, 2I] (gate | up), I % 16 == 0:
+/* SiLU-and-mul over gu [M, 2I] (gate | up), I % 16 == 0, I <= 32768:
  *   a = fp16(fp16(silu(gate)) * up) -> out [M, I] (may be NULL); aq/sa (may be NULL) its FP8 rows.
  * Replaces SiluAndMul (microserve/layers/activation.py:5-8) followed by
  * `_quantize_fp8_rows` of down_proj's input (microserve/layers/fp8_linear.py:71-73). */

@@ -107,6 +107,7 @@ int ms_rmsnorm(const void* x, const void* residual, const void* weight, int64_t 
   if (residual && !residual_out) return fail(MS_ERR_INVALID, "ms_rmsnorm: residual without residual_out");
   if ((yq == nullptr) != (sy == nullptr)) return fail(MS_ERR_INVALID, "ms_rmsnorm: yq and sy go together");
   if (H % 16 != 0) return fail(MS_ERR_UNSUPPORTED, "ms_rmsnorm: H=%lld is not a multiple of 16", (long long)H);
+  if (H > 32768) return fail(MS_ERR_UNSUPPORTED, "ms_rmsnorm: H=%lld > 32768", (long long)H);
   return check_cuda(ms::launch_rmsnorm(x, residual, weight, M, (int)H, eps, residual_out, y, yq, sy, S(stream)),
                     "ms_rmsnorm");
 }
@@ -117,6 +118,7 @@ int ms_silu_mul(const void* gu, int64_t M, int64_t I, void* out, void* aq, float
   if (!gu) return fail(MS_ERR_INVALID, "ms_silu_mul: null pointer");
   if ((aq == nullptr) != (sa == nullptr)) return fail(MS_ERR_INVALID, "ms_silu_mul: aq and sa go together");
   if (I % 16 != 0) return fail(MS_ERR_UNSUPPORTED, "ms_silu_mul: I=%lld is not a multiple of 16", (long long)I);
+  if (I > 32768) return fail(MS_ERR_UNSUPPORTED, "ms_silu_mul: I=%lld > 32768", (long long)I);
   return check_cuda(ms::launch_silu_mul(gu, M, (int)I, out, aq, sa, S(stream)), "ms_silu_mul");
 }
 
