@@ -125,8 +125,7 @@ __device__ __forceinline__ void tma_store_2d_wait(const CUtensorMap* map, uint32
 // Output of 16 token columns of one weight row n: y = fp16(fp16(v * sx * sw[n]) + bias[n]).
 // With `stage` the values go to a shared-memory tile [tokens][128 rows] fp16 (the
 // CTA then writes the tile with one bulk tensor store); without, straight to y
-// with one 2-byte store per token (64 bytes per warp instruction, which keeps a
-// tile's epilogue several microseconds long when it cannot overlap a main loop).
+// with one 2-byte store per token (64 bytes per warp instruction).
 __device__ __forceinline__ void out16(const GemmArgs& args, const float* v, const float* sx, float swn, float bn,
                                       int m0, int c0, int cols, int n, __half* stage, int row) {
   const float4* sxv = reinterpret_cast<const float4*>(sx + c0);
