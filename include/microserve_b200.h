@@ -75,6 +75,15 @@ int ms_quantize_rows_fp8(const void* x, int64_t ldx, int64_t M, int64_t K, void*
  * (microserve/layers/fp8_linear.py:26-45, :64-80). bias may be NULL.
  * workspace: at least ms_fp8_gemm_workspace_size(M, N, K) bytes (may be 0). */
 size_t ms_fp8_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/* The schedule ms_fp8_gemm uses for M x N x K on a GPU with `sms` SMs (host
+ * only, no GPU needed; for inspection and tests): plan[0] token-tile width BN
+ * (0 = the CUDA-core kernel for K % 16 != 0), plan[1] CTAs, plan[2] K parts
+ * per weight tile (split-K; 0 otherwise), plan[3] 1 for 256-row x 256-token
+ * tiles, plan[4] 1 for whole tiles (0: split-K or stream-K), plan[5] 128-byte
+ * K chunks per pipeline stage. No reference counterpart (the reference's
+ * `_fp8_mm` grid is fixed, microserve/layers/fp8_linear.py:75-77). */
+int ms_fp8_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* plan);
 int ms_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias, void* y,
                 int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
 

@@ -84,6 +84,13 @@ size_t ms_fp8_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
   return ms::gemm_workspace_bytes((int)M, (int)N, (int)K, num_sms());
 }
 
+int ms_fp8_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* plan) {
+  if (M <= 0 || N <= 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || sms <= 0 || !plan)
+    return fail(MS_ERR_INVALID, "ms_fp8_gemm_plan: bad arguments");
+  ms::gemm_plan((int)M, (int)N, (int)K, sms, plan);
+  return MS_OK;
+}
+
 int ms_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias, void* y,
                 int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
   if (M < 0 || N < 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)

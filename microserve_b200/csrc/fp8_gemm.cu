@@ -1004,10 +1004,21 @@ Plan make_plan(int M, int N, int K, int num_sms) {
 
 }  // namespace
 
-void gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* ctas_out) {
+void gemm_plan(int M, int N, int K, int num_sms, int* out) {
+  if (K % 16 != 0) {  // CUDA-core kernel: one thread per output, 128-column blocks
+    out[0] = 0;
+    out[1] = (int)((N + 127) / 128) * M;
+    out[2] = out[3] = out[5] = 0;
+    out[4] = 1;
+    return;
+  }
   const Plan p = make_plan(M, N, K, num_sms);
-  *bn_out = p.bn;
-  *ctas_out = p.ctas;
+  out[0] = p.bn;
+  out[1] = p.ctas;
+  out[2] = p.splits;
+  out[3] = p.wide;
+  out[4] = p.dp;
+  out[5] = p.ch;
 }
 
 size_t gemm_workspace_bytes(int M, int N, int K, int num_sms) {

@@ -45,7 +45,9 @@ size_t argmax_workspace_bytes(int64_t M);
 cudaError_t launch_argmax_rows(const void* x, int64_t M, int V, int64_t ldx, int64_t* idx, float* vmax,
                                void* workspace, cudaStream_t stream);
 
-void gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* ctas_out);
+// out[6]: token-tile width BN (0: CUDA-core kernel), CTAs, K parts per tile
+// (split-K, else 0), 256 x 256 tiles (0/1), whole tiles (0/1), K chunks per stage.
+void gemm_plan(int M, int N, int K, int num_sms, int* out);
 size_t gemm_workspace_bytes(int M, int N, int K, int num_sms);
 cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,
                             void* y, int M, int N, int K, void* workspace, size_t workspace_bytes, int num_sms,

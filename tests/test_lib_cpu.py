@@ -38,3 +38,45 @@ def test_bad_arguments_are_rejected_without_launch():
     assert lib.ms_fp8_gemm(None, None, None, None, None, None, 4, 4, 4, None, 0, None) == _lib.MS_ERR_INVALID
     assert b"null" in lib.ms_last_error()
     assert lib.ms_store_kv_fp8(None, None, 1, 8, 64, None, None, None, None, None, None) == _lib.MS_ERR_UNSUPPORTED
+
+
+def _plan(M, N, K, sms=148):
+    import ctypes as C
+    from microserve_b200 import _lib
+    out = (C.c_int * 6)()
+    assert _lib.load().ms_fp8_gemm_plan(M, N, K, sms, out) == 0
+    return dict(zip(("bn", "ctas", "splits", "wide", "dp", "ch"), list(out)))
+
+
+def test_gemm_schedules_of_the_8b_decode_and_prefill_shapes():
+    """The FP8 GEMM planner's choices for the bench's Qwen3-8B shapes on 148 SMs
+    (the rules in csrc/fp8_gemm.cu make_plan; timings behind them in
+    profiles/fp8_gemm_qwen3-8b_m256.md)."""
+    # decode, 256 tokens: qkv / o whole tiles of 96 / 64 tokens, one wave each
+    assert _plan(256, 6144, 4096) == dict(bn=96, ctas=144, splits=0, wide=0, dp=1, ch=2)
+    assert _plan(256, 4096, 4096) == dict(bn=64, ctas=128, splits=0, wide=0, dp=1, ch=2)
+    # gate_up: 96 tiles of 256 weight rows x 256 tokens
+    assert _plan(256, 24576, 4096) == dict(bn=256, ctas=96, splits=0, wide=1, dp=1, ch=1)
+    # down (long K): split-K, 32 weight tiles x 4 K parts
+    assert _plan(256, 4096, 12288) == dict(bn=256, ctas=128, splits=4, wide=0, dp=0, ch=2)
+    # one token: split-K with a 32-token tile, 3 K parts per weight tile
+    assert _plan(1, 6144, 4096) == dict(bn=32, ctas=144, splits=3, wide=0, dp=0, ch=2)
+    # prefill: 256-token tiles, whole tiles when they fill the SMs evenly
+    p = _plan(8192, 4096, 4096)
+    assert p["bn"] == 256 and p["dp"] == 1 and p["ctas"] == 148
+    # K % 16 != 0: the CUDA-core kernel
+    assert _plan(3, 70, 50)["bn"] == 0
+
+
+def test_gemm_schedules_keep_cooperating_ctas_resident():
+    """Split-K and stream-K CTAs wait for one another, so those schedules never
+    launch more CTAs than SMs; no K part is empty."""
+    for sms in (132, 148):
+        for M in (1, 16, 64, 100, 128, 160, 200, 256, 300, 1024, 4096):
+            for N, K in ((768, 4096), (4096, 512), (6144, 4096), (4096, 12288), (24576, 4096), (1000, 1040)):
+                p = _plan(M, N, K, sms)
+                if not p["dp"]:
+                    assert p["ctas"] <= sms, (M, N, K, sms, p)
+                if p["splits"]:
+                    steps = -(-K // (128 * p["ch"]))
+                    assert 2 <= p["splits"] <= steps, (M, N, K, sms, p)
