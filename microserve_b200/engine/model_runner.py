@@ -17,6 +17,8 @@ Differences, all host-side or scheduling-neutral:
 """
 from __future__ import annotations
 
+import itertools
+
 import numpy as np
 import torch
 
@@ -176,22 +178,28 @@ class ModelRunner:
         return bt[positions // self.block_size] * self.block_size + positions % self.block_size
 
     def _tables(self, seqs: list[Sequence], width: int | None = None) -> np.ndarray:
-        width = width or max(len(s.block_table) for s in seqs)
-        bt = np.full((len(seqs), width), -1, dtype=np.int32)
-        for i, s in enumerate(seqs):
-            bt[i, :len(s.block_table)] = s.block_table
+        """Block tables as rows of int32, padded with -1 (one flat copy, no per-row writes)."""
+        n = len(seqs)
+        lens = np.fromiter((len(s.block_table) for s in seqs), dtype=np.int64, count=n)
+        width = width or int(lens.max())
+        flat = np.fromiter(itertools.chain.from_iterable(s.block_table for s in seqs), dtype=np.int32,
+                           count=int(lens.sum()))
+        bt = np.full((n, width), -1, dtype=np.int32)
+        bt[np.arange(width)[None, :] < lens[:, None]] = flat
         return bt
 
     def prepare_decode(self, seqs: list[Sequence]):
-        """Host arrays of a decode batch: ids, positions, slots (int64), seqlens, tables (int32)."""
-        pos = np.array([s.num_computed_tokens for s in seqs], dtype=np.int64)
-        for s in seqs:
-            assert s.gap == 1 and s.num_scheduled_tokens == 1
-        ids = np.array([s.token_ids[s.num_computed_tokens] for s in seqs], dtype=np.int64)
+        """Host arrays of a decode batch: ids, positions, slots (int64), seqlens, tables (int32).
+        slot = block_table[p // block_size] * block_size + p % block_size (model_runner.py:135-136
+        of the reference), read from the padded table of the batch."""
+        n = len(seqs)
+        assert all(s.gap == 1 and s.num_scheduled_tokens == 1 for s in seqs)
+        pos = np.fromiter((s.num_computed_tokens for s in seqs), dtype=np.int64, count=n)
+        ids = np.fromiter((s.token_ids[s.num_computed_tokens] for s in seqs), dtype=np.int64, count=n)
+        bt = self._tables(seqs)
         bs = self.block_size
-        slots = np.array([s.block_table[p // bs] * bs + p % bs for s, p in zip(seqs, pos.tolist())],
-                         dtype=np.int64)
-        return ids, pos, slots, (pos + 1).astype(np.int32), self._tables(seqs)
+        slots = bt[np.arange(n), pos // bs].astype(np.int64) * bs + pos % bs
+        return ids, pos, slots, (pos + 1).astype(np.int32), bt
 
     def prepare_prefill(self, seqs: list[Sequence]):
         ids, pos, slots, cu = [], [], [], [0]
