@@ -144,9 +144,10 @@ int ms_paged_decode_fp8(const void* q, const void* k_cache, const void* v_cache,
  * stream). The context-split partials go to a 4 MiB buffer built into the
  * library, which every GPU that loads the library keeps until exit; batches
  * needing more return MS_ERR_UNSUPPORTED (use ms_paged_decode_fp8). The first
- * call on a device looks up the buffer's device address, so make it before
- * any stream capture. All calls on a device share the buffer: calls that
- * overlap on the GPU race and must be serialised by the caller. */
+ * call on a device (and the first after the device's context was destroyed and
+ * recreated, e.g. by cudaDeviceReset) looks up the buffer's device address, so
+ * make it before any stream capture. All calls on a device share the buffer:
+ * calls that overlap on the GPU race and must be serialised by the caller. */
 int ms_paged_decode_fp8_noalloc(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
                                 const float* v_scale, const int32_t* seqlens, const int32_t* block_tables, void* out,
                                 int B, int Hq, int Hkv, int head_dim, int block_size, int max_blocks,
@@ -195,23 +196,62 @@ int ms_ipc_handle(const void* ptr, void* handle, int64_t* offset);
 int ms_ipc_open(const void* handle, int64_t offset, void** base_out, void** ptr_out);
 int ms_ipc_close(void* base);
 
+/* Byte offsets inside one rank's communication buffer for the fused op below
+ * (world ranks, hidden size H, at most max_rows rows per call):
+ *   offsets[0] partial   [max_rows, H] fp16  this rank's row-parallel output (the GEMM's out)
+ *   offsets[1] recv      receive slots peers write (internal)
+ *   offsets[2] gather_q  [max_rows, H] e4m3  every rank's normalised rows, FP8 codes
+ *   offsets[3] gather_s  [max_rows] fp32     their scales
+ *   offsets[4] gather_h  [max_rows, H] fp16  normalised fp16 rows (want_fp16 calls)
+ *   offsets[5] control words, offsets[6] total bytes.
+ * No reference counterpart (plumbing of the op below). */
+int ms_tp_layout(int world, int64_t hidden, int64_t max_rows, int64_t* offsets);
+
+/* Puts one rank's buffer (ms_tp_layout total bytes, 256-byte aligned) in its
+ * initial state: every byte 0xFF ("not yet written") except the control words
+ * (zero). Call once per rank, before the buffer is shared, with the stream
+ * synchronised before any peer's first call. */
+int ms_tp_buffer_init(void* base, int world, int64_t hidden, int64_t max_rows, void* stream);
+
 /* Row-parallel all-reduce + residual add + RMSNorm + FP8 row quantisation, one
- * kernel per rank. partial[p], gather_q[p], gather_s[p], gather_h[p] (optional)
- * and flags[p] are rank p's buffers as mapped in this process: partial = rank p's
- * row-parallel output [M, H] fp16; gather_q/gather_s = [M, H] e4m3 / [M] fp32
- * that receive every rank's rows; gather_h = [M, H] fp16 rows (the final norm);
- * flags = [2 * world] int32, zero before the first call. ctrl: this rank's
- * [2] int32 (zero before the first call). Rank r reduces and normalises rows
- * [r * R, (r + 1) * R), R = ceil(M / world), updating those rows of its residual
- * [M, H] in place, and writes them to every rank; the kernel returns after every
- * rank's rows are in this rank's gather buffers. Replaces RowParallelLinear's
- * dist.all_reduce (microserve/layers/linear.py:70-77) + the add/RMSNorm that
- * follows (layers/layernorm.py:22-42) + the next FP8 activation quantisation
- * (layers/fp8_linear.py:14-23). world <= 8, H % 8 == 0, H <= 16384. */
-int ms_tp_allreduce_rmsnorm_fp8(const void* const* partial, void* const* gather_q, float* const* gather_s,
-                                void* const* gather_h, int* const* flags, int* ctrl, void* residual,
-                                const void* weight, int rank, int world, int64_t M, int64_t H, float eps,
+ * kernel per rank. bases[p] = rank p's communication buffer as mapped in this
+ * process (CUDA IPC; bases[rank] is the local one). The rank's row-parallel
+ * output [M, H] fp16 is read from its partial area. With R = ceil(M / world),
+ * rank r owns rows [r R, (r + 1) R): it sums those rows of every rank's output
+ * in rank order (fp32, rounded to fp16 once), adds its residual rows (updated
+ * in place, fp16), normalises them (weight [H] fp16, eps) and writes codes +
+ * scales (and, with want_fp16, the fp16 rows) into every rank's gather area;
+ * the call returns (on the GPU) once every rank's rows are in this rank's
+ * gather area. Rows of the residual that the rank does not own are neither
+ * read nor written. Readiness is carried by the data (no flags); every wait is
+ * bounded (ms_set_wait_limit) and a wait that runs out records status 2 (peer
+ * timeout, ms_get_device_status), after which the buffers of the whole group
+ * must be re-initialised. Every rank makes the same sequence of calls.
+ * Replaces RowParallelLinear's dist.all_reduce (microserve/layers/linear.py:70-77)
+ * + the add/RMSNorm that follows (layers/layernorm.py:22-42) + the next FP8
+ * activation quantisation (layers/fp8_linear.py:14-23).
+ * world <= 8, H % 16 == 0, H <= 16384, 0 <= M <= max_rows. */
+int ms_tp_allreduce_rmsnorm_fp8(void* const* bases, int rank, int world, int64_t hidden, int64_t max_rows,
+                                void* residual, const void* weight, int64_t M, float eps, int want_fp16,
                                 void* stream);
+
+/* Upper bound, in nanoseconds, of every in-kernel wait on the current device
+ * (peer data, pipeline barriers); default 4e9. A wait that runs out records a
+ * device status and the kernel returns. Set it outside stream capture; it
+ * applies to launches made after the call. No reference counterpart (the
+ * reference has only host asserts, microserve/engine/llm.py:43-49). */
+int ms_set_wait_limit(uint64_t ns);
+
+/* Per-row absolute maximum of fp16 rows: amax[m] = max_k |x[m, k]| (fp32).
+ * With ms_quantize_rows_fp8_amax it gives the exact row scales of a K-sharded
+ * activation (an all-reduce max of amax between the two calls): the scale the
+ * reference computes over the full row (microserve/layers/fp8_linear.py:20). */
+int ms_row_amax(const void* x, int64_t ldx, int64_t M, int64_t K, float* amax, void* stream);
+
+/* ms_quantize_rows_fp8 with the row amax given (scale = max(amax[m], 1e-8)
+ * * fl32(1/448)) instead of taken over the K columns passed. */
+int ms_quantize_rows_fp8_amax(const void* x, int64_t ldx, int64_t M, int64_t K, const float* amax, void* xq,
+                              float* sx, void* stream);
 
 #ifdef __cplusplus
 }

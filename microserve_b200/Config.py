@@ -6,6 +6,10 @@
                          row-parallel outputs with this library's peer-memory
                          kernel fused with add + RMSNorm + FP8 quantisation
                          (utils/tp_fused.py) instead of NCCL all-reduce;
+  tp_exact_act_scale   - with tensor parallelism, scale each row-parallel
+                         input row (o_proj, down_proj) by its amax over the
+                         full row, as a single GPU does (one all-reduce max of
+                         a float per row), instead of the local shard's amax;
   load_format          - "safetensors" (model_dir holds the checkpoint) or
                          "dummy" (seeded N(0, 0.02) random weights of the
                          shape in model_dir/config.json or `hf_config`);
@@ -40,6 +44,7 @@ class Config:
     scheduler_policy: str = "mixed"
     tensor_parallel_size: int = 1
     tp_fused_collective: bool = True
+    tp_exact_act_scale: bool = False
     load_format: str = "safetensors"
     hf_config: object = None
 

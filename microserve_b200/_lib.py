@@ -28,7 +28,12 @@ SIGNATURES: dict[str, tuple] = {
     "ms_ipc_handle": (i32, [vp, vp, C.POINTER(C.c_int64)]),
     "ms_ipc_open": (i32, [vp, i64, C.POINTER(vp), C.POINTER(vp)]),
     "ms_ipc_close": (i32, [vp]),
-    "ms_tp_allreduce_rmsnorm_fp8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i64, i64, f32, vp]),
+    "ms_tp_layout": (i32, [i32, i64, i64, C.POINTER(C.c_int64)]),
+    "ms_tp_buffer_init": (i32, [vp, i32, i64, i64, vp]),
+    "ms_tp_allreduce_rmsnorm_fp8": (i32, [vp, i32, i32, i64, i64, vp, vp, i64, f32, i32, vp]),
+    "ms_set_wait_limit": (i32, [C.c_uint64]),
+    "ms_row_amax": (i32, [vp, i64, i64, i64, vp, vp]),
+    "ms_quantize_rows_fp8_amax": (i32, [vp, i64, i64, i64, vp, vp, vp, vp]),
     "ms_argmax_rows": (i32, [vp, i64, i64, i64, vp, vp, vp, sz, vp]),
     "ms_get_device_status": (i32, [C.POINTER(C.c_int), vp]),
     "ms_quantize_rows_fp8": (i32, [vp, i64, i64, i64, vp, vp, vp]),
@@ -96,3 +101,23 @@ def device_status() -> int:
     s = C.c_int(0)
     check(load().ms_get_device_status(C.byref(s), stream_ptr()), "ms_get_device_status")
     return s.value
+
+
+STATUS_NAMES = {1: "a pipeline barrier wait timed out", 2: "a peer (tensor-parallel rank) did not answer in time"}
+
+
+class DeviceWaitTimeout(RuntimeError):
+    """A bounded in-kernel wait ran out (ms_get_device_status != 0): results of
+    the step are invalid; with tensor parallelism the group must be rebuilt."""
+
+
+def raise_on_device_status(where: str) -> None:
+    """Read (and clear) the device status word; raise DeviceWaitTimeout if set."""
+    s = device_status()
+    if s != 0:
+        raise DeviceWaitTimeout(f"{where}: device status {s} ({STATUS_NAMES.get(s, 'unknown')})")
+
+
+def set_wait_limit(seconds: float) -> None:
+    """Upper bound of every in-kernel wait on the current device (default 4 s)."""
+    check(load().ms_set_wait_limit(max(1, int(seconds * 1e9))), "ms_set_wait_limit")

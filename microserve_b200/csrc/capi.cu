@@ -309,22 +309,64 @@ int ms_ipc_close(void* base) {
   return check_cuda(cudaIpcCloseMemHandle(base), "ms_ipc_close");
 }
 
-int ms_tp_allreduce_rmsnorm_fp8(const void* const* partial, void* const* gather_q, float* const* gather_s,
-                                void* const* gather_h, int* const* flags, int* ctrl, void* residual,
-                                const void* weight, int rank, int world, int64_t M, int64_t H, float eps,
+int ms_tp_layout(int world, int64_t hidden, int64_t max_rows, int64_t* offsets) {
+  if (world < 1 || world > 8 || hidden <= 0 || max_rows <= 0 || !offsets)
+    return fail(MS_ERR_INVALID, "ms_tp_layout: bad arguments");
+  const ms::TpLayout l = ms::tp_layout(world, hidden, max_rows);
+  const int64_t o[7] = {l.partial, l.recv, l.gq, l.gs, l.gh, l.ctrl, l.total};
+  memcpy(offsets, o, sizeof(o));
+  return MS_OK;
+}
+
+int ms_tp_buffer_init(void* base, int world, int64_t hidden, int64_t max_rows, void* stream) {
+  if (!base || world < 1 || world > 8 || hidden <= 0 || max_rows <= 0)
+    return fail(MS_ERR_INVALID, "ms_tp_buffer_init: bad arguments");
+  if (((uintptr_t)base & 255) != 0) return fail(MS_ERR_INVALID, "ms_tp_buffer_init: base not 256-byte aligned");
+  return check_cuda(ms::launch_tp_buffer_init(base, world, hidden, max_rows, S(stream)), "ms_tp_buffer_init");
+}
+
+int ms_tp_allreduce_rmsnorm_fp8(void* const* bases, int rank, int world, int64_t hidden, int64_t max_rows,
+                                void* residual, const void* weight, int64_t M, float eps, int want_fp16,
                                 void* stream) {
-  if (world < 1 || world > 8 || rank < 0 || rank >= world || M < 0 || M > INT32_MAX || H <= 0 || H % 8 != 0 ||
-      H > 16384)
-    return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: bad sizes rank=%d world=%d M=%lld H=%lld", rank,
-                world, (long long)M, (long long)H);
-  if (!partial || !gather_q || !gather_s || !flags || !ctrl || !residual || !weight)
-    return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: null pointer");
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || M < 0 || max_rows <= 0 || M > max_rows ||
+      max_rows > INT32_MAX || hidden <= 0)
+    return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: bad sizes rank=%d world=%d M=%lld max_rows=%lld", rank,
+                world, (long long)M, (long long)max_rows);
+  if (hidden % 16 != 0 || hidden > 16384)
+    return fail(MS_ERR_UNSUPPORTED, "ms_tp_allreduce_rmsnorm_fp8: hidden=%lld (needs a multiple of 16, <= 16384)",
+                (long long)hidden);
+  if (M == 0) return MS_OK;
+  if (!bases || !residual || !weight) return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: null pointer");
   for (int p = 0; p < world; ++p)
-    if (!partial[p] || !gather_q[p] || !gather_s[p] || !flags[p] || (gather_h && !gather_h[p]))
-      return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: null peer pointer (rank %d)", p);
-  return check_cuda(ms::launch_tp_allreduce_rmsnorm_fp8(partial, gather_q, gather_s, gather_h, flags, ctrl, residual,
-                                                        weight, rank, world, (int)M, (int)H, eps, S(stream)),
+    if (!bases[p] || ((uintptr_t)bases[p] & 255) != 0)
+      return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: buffer of rank %d null or not 256-byte aligned", p);
+  if (((uintptr_t)residual & 15) != 0 || ((uintptr_t)weight & 15) != 0)
+    return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: residual/weight not 16-byte aligned");
+  return check_cuda(ms::launch_tp_allreduce_rmsnorm_fp8(bases, rank, world, hidden, max_rows, residual, weight,
+                                                        (int)M, eps, want_fp16, num_sms(), S(stream)),
                     "ms_tp_allreduce_rmsnorm_fp8");
+}
+
+int ms_set_wait_limit(uint64_t ns) {
+  if (ns == 0) return fail(MS_ERR_INVALID, "ms_set_wait_limit: limit must be > 0");
+  const unsigned long long v = ns;
+  return check_cuda(cudaMemcpyToSymbol(ms::g_wait_limit_ns, &v, sizeof(v)), "ms_set_wait_limit");
+}
+
+int ms_row_amax(const void* x, int64_t ldx, int64_t M, int64_t K, float* amax, void* stream) {
+  if (M < 0 || K <= 0 || ldx < K || K > (1 << 20)) return fail(MS_ERR_INVALID, "ms_row_amax: bad sizes");
+  if (M == 0) return MS_OK;
+  if (!x || !amax) return fail(MS_ERR_INVALID, "ms_row_amax: null pointer");
+  return check_cuda(ms::launch_row_amax(x, ldx, M, (int)K, amax, S(stream)), "ms_row_amax");
+}
+
+int ms_quantize_rows_fp8_amax(const void* x, int64_t ldx, int64_t M, int64_t K, const float* amax, void* xq,
+                              float* sx, void* stream) {
+  if (M < 0 || K <= 0 || ldx < K || K > (1 << 20)) return fail(MS_ERR_INVALID, "ms_quantize_rows_fp8_amax: bad sizes");
+  if (M == 0) return MS_OK;
+  if (!x || !amax || !xq || !sx) return fail(MS_ERR_INVALID, "ms_quantize_rows_fp8_amax: null pointer");
+  return check_cuda(ms::launch_quantize_rows_amax(x, ldx, M, (int)K, amax, xq, sx, S(stream)),
+                    "ms_quantize_rows_fp8_amax");
 }
 
 }  // extern "C"

@@ -214,21 +214,27 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Upper bound of any in-kernel wait. Legitimate waits last microseconds to
-// milliseconds; this only ends a wait whose event can no longer come.
-constexpr uint64_t kWaitLimitNs = 4000000000ull;
+// Upper bound of any in-kernel wait, per device (ms_set_wait_limit). Legitimate
+// waits last microseconds to milliseconds; the limit only ends a wait whose
+// event can no longer come (a peer that died or never joined). Default 4 s.
+constexpr uint64_t kDefaultWaitLimitNs = 4000000000ull;
+extern __device__ unsigned long long g_wait_limit_ns;
+
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+  return *static_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+}
 
 // Wait until the barrier's phase `phase` completed. try_wait already suspends
 // the thread in hardware until the phase completes (or a short time limit
 // passes), so the loop adds no sleep of its own: a __nanosleep here delays the
-// wake-up by its own granularity. Gives up after kWaitLimitNs, records
+// wake-up by its own granularity. Gives up after wait_limit_ns(), records
 // kStatusMbarTimeout and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
   if (mbar_try_wait(bar, phase)) return true;
-  const uint64_t t0 = global_ns();
+  const uint64_t t0 = global_ns(), limit = wait_limit_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, phase)) return true;
-    if ((i & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) break;
+    if ((i & 255u) == 0 && global_ns() - t0 > limit) break;
   }
   set_device_status(kStatusMbarTimeout);
   return false;

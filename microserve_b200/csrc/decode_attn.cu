@@ -497,21 +497,39 @@ size_t decode_noalloc_scratch_bytes() { return kNoAllocScratchBytes; }
 
 // Device address of the built-in scratch on the current device. Host code
 // cannot use the symbol itself (it names a host-side stand-in), so the
-// address is looked up once per device, with that device current; the first
-// call on a device therefore must not happen during stream capture.
+// address is looked up with that device current and cached per device and
+// CUDA context: after a context is destroyed and recreated (cudaDeviceReset)
+// the next call looks it up again. A look-up (the first call on a device, or
+// the first after a reset) must not happen during stream capture.
 cudaError_t decode_noalloc_scratch(void** ptr) {
+  typedef CUresult (*CtxFn)(CUcontext*);
   static std::mutex mu;
   static void* addr[64] = {};
+  static CUcontext ctx_of[64] = {};
+  static CtxFn ctx_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      ctx_fn = reinterpret_cast<CtxFn>(f);
+  });
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (ctx_fn == nullptr) return cudaErrorUnknown;
+  CUcontext ctx = nullptr;
+  if (ctx_fn(&ctx) != CUDA_SUCCESS) return cudaErrorUnknown;
   std::lock_guard<std::mutex> g(mu);
-  if (addr[dev] == nullptr) {
+  if (ctx == nullptr || addr[dev] == nullptr || ctx_of[dev] != ctx) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // also makes the device's context current
     if (e != cudaSuccess) return e;
+    if (ctx_fn(&ctx) != CUDA_SUCCESS) return cudaErrorUnknown;
     addr[dev] = p;
+    ctx_of[dev] = ctx;
   }
   *ptr = addr[dev];
   return cudaSuccess;

@@ -302,7 +302,7 @@ __device__ __forceinline__ void split_epilogue(const GemmArgs& args, uint32_t ac
     const uint64_t t0 = global_ns();
     uint32_t spins = 0;
     while (ld_acquire(cnt) < S) {
-      if ((++spins & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+      if ((++spins & 255u) == 0 && global_ns() - t0 > wait_limit_ns()) {
         set_device_status(kStatusMbarTimeout);
         break;
       }
@@ -544,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = c_first; c <= c_last; ++c) {
             uint32_t spins = 0;
             while (ld_acquire(&args.flags[c]) == 0) {
-              if ((++spins & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+              if ((++spins & 255u) == 0 && global_ns() - t0 > wait_limit_ns()) {
                 set_device_status(kStatusMbarTimeout);
                 break;
               }

@@ -8,6 +8,11 @@ namespace ms {
 
 cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t M, int K, void* xq, float* sx,
                                  cudaStream_t stream);
+// Per-row amax of fp16 rows, and row quantisation with a given amax (exact scales
+// of K-sharded rows after an all-reduce max).
+cudaError_t launch_row_amax(const void* x, int64_t ldx, int64_t M, int K, float* amax, cudaStream_t stream);
+cudaError_t launch_quantize_rows_amax(const void* x, int64_t ldx, int64_t M, int K, const float* amax, void* xq,
+                                      float* sx, cudaStream_t stream);
 cudaError_t launch_rmsnorm(const void* x, const void* residual, const void* weight, int64_t M, int H, float eps,
                            void* residual_out, void* y, void* yq, float* sy, cudaStream_t stream);
 cudaError_t launch_silu_mul(const void* gu, int64_t M, int I, void* out, void* aq, float* sa, cudaStream_t stream);
@@ -36,10 +41,15 @@ cudaError_t launch_prefill_attention(bool paged, const void* q, const void* k16,
                                      int head_dim, int block_size, int max_blocks, float softmax_scale,
                                      cudaStream_t stream);
 
-cudaError_t launch_tp_allreduce_rmsnorm_fp8(const void* const* partial, void* const* gather_q,
-                                            float* const* gather_s, void* const* gather_h, int* const* flags,
-                                            int* ctrl, void* residual, const void* weight, int rank, int world,
-                                            int M, int H, float eps, cudaStream_t stream);
+// One rank's communication buffer for the fused tensor-parallel op: byte offsets.
+struct TpLayout {
+  int64_t partial, recv, gq, gs, gh, ctrl, total;
+};
+TpLayout tp_layout(int world, int64_t H, int64_t max_rows);
+cudaError_t launch_tp_buffer_init(void* base, int world, int64_t H, int64_t max_rows, cudaStream_t stream);
+cudaError_t launch_tp_allreduce_rmsnorm_fp8(void* const* bases, int rank, int world, int64_t H, int64_t max_rows,
+                                            void* residual, const void* weight, int M, float eps, int want_h,
+                                            int num_sms, cudaStream_t stream);
 
 size_t argmax_workspace_bytes(int64_t M);
 cudaError_t launch_argmax_rows(const void* x, int64_t M, int V, int64_t ldx, int64_t* idx, float* vmax,

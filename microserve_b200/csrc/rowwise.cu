@@ -13,15 +13,12 @@
 //   SiLU*mul           layers/activation.py:5-8     (silu in fp32 -> fp16, then fp16 multiply)
 #include "common.cuh"
 #include "kernels.h"
+#include "rowops.cuh"
 
 namespace ms {
 namespace {
 
 constexpr int kRowThreads = 512;
-
-struct alignas(16) H8 {
-  __half2 h[4];
-};
 
 // x: [M, K] fp16 with row stride ldx (elements), any K and alignment (scalar
 // loads and stores; irregular layer widths). Writes xq [M, K] e4m3 and sx [M].
@@ -60,9 +57,6 @@ __global__ void __launch_bounds__(kRowThreads) quantize_rows_scalar_kernel(const
 // spent about a microsecond in each block-wide reduction). FP8 codes use
 // div_by_rcp: the IEEE quotient x / scale in five flops.
 // ---------------------------------------------------------------------------
-constexpr int kMaxRowWarps = 16;
-constexpr int kRowVec = 8;  // 16-byte vectors per thread at most
-
 // Reduction over the T threads of the CTA's row (red: a distinct shared array
 // of kMaxRowWarps floats per reduction, so none is reused).
 template <int W, bool kMax>
@@ -80,45 +74,14 @@ __device__ __forceinline__ float group_reduce(float v, float* red, int t) {
   }
 }
 
-__device__ __forceinline__ H8 ld_h8(const __half* p) {
-  const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p));
-  H8 h;
-  memcpy(&h, &u, sizeof(h));
-  return h;
-}
-__device__ __forceinline__ void st_h8(__half* p, const H8& h) {
-  uint4 u;
-  memcpy(&u, &h, sizeof(u));
-  *reinterpret_cast<uint4*>(p) = u;
-}
-
-// Eight fp16 values -> eight e4m3 codes (x / s rounded as the IEEE quotient, r = 1/s).
-__device__ __forceinline__ uint2 encode8(const H8& a, float s, float r) {
-  uint32_t w[2];
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    const float2 f0 = __half22float2(a.h[2 * p]);
-    const float2 f1 = __half22float2(a.h[2 * p + 1]);
-    const uint16_t lo = f32x2_to_e4m3x2(div_by_rcp(f0.x, s, r), div_by_rcp(f0.y, s, r));
-    const uint16_t hi = f32x2_to_e4m3x2(div_by_rcp(f1.x, s, r), div_by_rcp(f1.y, s, r));
-    w[p] = (uint32_t)lo | ((uint32_t)hi << 16);
-  }
-  return make_uint2(w[0], w[1]);
-}
-
-__device__ __forceinline__ float amax8(const H8& a, float amax) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 f = __half22float2(a.h[j]);
-    amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-  }
-  return amax;
-}
-
 // Per-row FP8 quantisation (16-byte aligned rows, K % 16 == 0, K / 8 <= kRowVec * T).
+// amax_in: row amax given (exact scales of a K-sharded row); amax_out: write the
+// row amax and nothing else.
 template <int W>
 __global__ void __launch_bounds__(32 * W) quantize_rows_group_kernel(const __half* __restrict__ x, int64_t ldx, int K,
-                                                                    uint8_t* __restrict__ xq, float* __restrict__ sx) {
+                                                                    uint8_t* __restrict__ xq, float* __restrict__ sx,
+                                                                    const float* __restrict__ amax_in,
+                                                                    float* __restrict__ amax_out) {
   __shared__ float red_max[kMaxRowWarps];
   constexpr int T = 32 * W;
   const int t = threadIdx.x;
@@ -136,6 +99,11 @@ __global__ void __launch_bounds__(32 * W) quantize_rows_group_kernel(const __hal
   for (int i = 0; i < kRowVec; ++i)
     if (t + i * T < nv) amax = amax8(a[i], amax);
   amax = group_reduce<W, true>(amax, red_max, t);
+  if (amax_out != nullptr) {
+    if (t == 0) amax_out[m] = amax;
+    return;
+  }
+  if (amax_in != nullptr) amax = amax_in[m];
   const float scale = fp8_scale_from_amax(amax), rcp = 1.0f / scale;
   uint8_t* dst = xq + m * (int64_t)K;
 #pragma unroll
@@ -189,29 +157,17 @@ __global__ void __launch_bounds__(32 * W) rmsnorm_group_kernel(const __half* __r
       }
     }
   }
-  float ss = 0.f;
+  float ss = 0.f;  // the canonical sum of squares (rowops.cuh), shared with the TP op
 #pragma unroll
-  for (int i = 0; i < kRowVec; ++i) {
-    if (t + i * T < nv) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __half22float2(a[i].h[j]);
-        ss += f.x * f.x + f.y * f.y;
-      }
-    }
-  }
+  for (int i = 0; i < kRowVec; ++i)
+    if (t + i * T < nv) ss = sumsq8(a[i], ss);
   ss = group_reduce<W, false>(ss, red_ss, t);
   const float inv = rsqrtf(ss / (float)H + eps);
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < kRowVec; ++i) {
     if (t + i * T < nv) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __half22float2(a[i].h[j]);
-        const __half2 n = __floats2half2_rn(f.x * inv, f.y * inv);
-        a[i].h[j] = __hmul2(n, w[i].h[j]);
-      }
+      a[i] = norm8(a[i], w[i], inv);
       amax = amax8(a[i], amax);
       if (y != nullptr) st_h8(y + base + (t + i * T) * 8, a[i]);
     }
@@ -286,14 +242,6 @@ inline int row_threads(int K) {
   return t < kRowThreads ? (t < 32 ? 32 : t) : kRowThreads;
 }
 
-// Warps per row so that a thread holds at most kRowVec 16-byte vectors (a power
-// of two, <= kMaxRowWarps); 0 if the row is too long.
-inline int row_warps(int nv) {
-  int w = 1;
-  while (w * 32 * kRowVec < nv && w < kMaxRowWarps) w <<= 1;
-  return w * 32 * kRowVec >= nv ? w : 0;
-}
-
 #define MS_ROW_SWITCH(w, CALL) \
   switch (w) {                 \
     case 1: return CALL(1);    \
@@ -315,7 +263,7 @@ cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t M, int K, v
   if (vec && row_warps(K / 8) > 0) {
 #define MS_CALL(W)                                                                                      \
   launch_kernel(quantize_rows_group_kernel<W>, dim3((unsigned)M), dim3(32 * W), 0, stream, (const __half*)x, \
-                ldx, K, (uint8_t*)xq, sx)
+                ldx, K, (uint8_t*)xq, sx, (const float*)nullptr, (float*)nullptr)
     MS_ROW_SWITCH(row_warps(K / 8), MS_CALL)
 #undef MS_CALL
   } else {
@@ -323,6 +271,31 @@ cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t M, int K, v
     return launch_kernel(quantize_rows_scalar_kernel, dim3((unsigned)M), dim3(row_threads(K)), smem, stream,
                          (const __half*)x, ldx, K, (uint8_t*)xq, sx);
   }
+}
+
+static bool rows_vectorised(const void* x, int64_t ldx, int K) {
+  return (K % 16 == 0) && (ldx % 8 == 0) && (((uintptr_t)x & 15) == 0) && row_warps(K / 8) > 0;
+}
+
+cudaError_t launch_row_amax(const void* x, int64_t ldx, int64_t M, int K, float* amax, cudaStream_t stream) {
+  if (M == 0) return cudaSuccess;
+  if (!rows_vectorised(x, ldx, K)) return cudaErrorInvalidValue;
+#define MS_CALL(W)                                                                                      \
+  launch_kernel(quantize_rows_group_kernel<W>, dim3((unsigned)M), dim3(32 * W), 0, stream, (const __half*)x, \
+                ldx, K, (uint8_t*)nullptr, (float*)nullptr, (const float*)nullptr, amax)
+  MS_ROW_SWITCH(row_warps(K / 8), MS_CALL)
+#undef MS_CALL
+}
+
+cudaError_t launch_quantize_rows_amax(const void* x, int64_t ldx, int64_t M, int K, const float* amax, void* xq,
+                                      float* sx, cudaStream_t stream) {
+  if (M == 0) return cudaSuccess;
+  if (!rows_vectorised(x, ldx, K) || ((uintptr_t)xq & 15) != 0) return cudaErrorInvalidValue;
+#define MS_CALL(W)                                                                                      \
+  launch_kernel(quantize_rows_group_kernel<W>, dim3((unsigned)M), dim3(32 * W), 0, stream, (const __half*)x, \
+                ldx, K, (uint8_t*)xq, sx, amax, (float*)nullptr)
+  MS_ROW_SWITCH(row_warps(K / 8), MS_CALL)
+#undef MS_CALL
 }
 
 cudaError_t launch_rmsnorm(const void* x, const void* residual, const void* weight, int64_t M, int H, float eps,

@@ -3,6 +3,7 @@
 
 namespace ms {
 __device__ int g_device_status = 0;
+__device__ unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 std::atomic<long long> g_host_launches{0};
 std::atomic<int> g_pdl_enabled{1};
 }  // namespace ms

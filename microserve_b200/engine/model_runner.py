@@ -23,7 +23,7 @@ import numpy as np
 import torch
 
 from microserve_b200.Config import Config
-from microserve_b200 import kernels
+from microserve_b200 import _lib, kernels
 from microserve_b200.engine.sequence import Sequence
 from microserve_b200.layers.attention import Attention
 from microserve_b200.layers.fp8_linear import quantize_fp8_linears
@@ -85,6 +85,7 @@ class ModelRunner:
             raise RuntimeError(f"tensor_parallel_size={config.tensor_parallel_size} but the process group has "
                                f"{tp.tp_size()} ranks (call utils.dist.init_tensor_parallel first)")
 
+        tp.set_exact_act_scale(config.tp_exact_act_scale)
         self.hf_config = hf = _load_hf_config(config)
         self.num_kv_heads = hf.num_key_value_heads // tp.tp_size()
         self.head_dim = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
@@ -198,7 +199,10 @@ class ModelRunner:
         ids = np.fromiter((s.token_ids[s.num_computed_tokens] for s in seqs), dtype=np.int64, count=n)
         bt = self._tables(seqs)
         bs = self.block_size
-        slots = bt[np.arange(n), pos // bs].astype(np.int64) * bs + pos % bs
+        blk = bt[np.arange(n), pos // bs]
+        if (blk < 0).any():
+            raise RuntimeError("decode position beyond the sequence's allocated blocks")
+        slots = blk.astype(np.int64) * bs + pos % bs
         return ids, pos, slots, (pos + 1).astype(np.int32), bt
 
     def prepare_prefill(self, seqs: list[Sequence]):
@@ -337,6 +341,9 @@ class ModelRunner:
             for i in hot:
                 tokens[i] = self._sample_one(full[i], seqs[i].sampling_params)
         host = tokens.to("cpu").tolist()
+        # the copy above synchronised the stream: a bounded in-kernel wait that ran out
+        # during this step (a peer rank that died or fell out of step) makes it invalid
+        _lib.raise_on_device_status("model step")
         return [host[i] if s.needs_sample else None for i, s in enumerate(seqs)]
 
     def _sample_one(self, row: torch.Tensor, p) -> torch.Tensor:

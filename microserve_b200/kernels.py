@@ -74,6 +74,38 @@ def quantize_rows_fp8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return xq, sx
 
 
+def row_amax(x: torch.Tensor) -> torch.Tensor:
+    """x [M, K] fp16 -> amax [M] fp32, the per-row absolute maximum."""
+    _cuda(x, "x")
+    if x.dtype != torch.float16:
+        raise ValueError("row_amax requires fp16 input")
+    x2 = x if x.dim() == 2 else x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M, K = x2.shape
+    amax = torch.empty((M,), dtype=torch.float32, device=x.device)
+    check(_lib.load().ms_row_amax(ptr(x2), x2.stride(0), M, K, ptr(amax), stream_ptr()), "ms_row_amax")
+    return amax
+
+
+def quantize_rows_fp8_amax(x: torch.Tensor, amax: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """quantize_rows_fp8 with the row amax given (scale = max(amax, 1e-8) * fl32(1/448))."""
+    _cuda(x, "x")
+    if x.dtype != torch.float16 or amax.dtype != torch.float32:
+        raise ValueError("quantize_rows_fp8_amax requires fp16 rows and fp32 amax")
+    x2 = x if x.dim() == 2 else x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M, K = x2.shape
+    if amax.shape != (M,):
+        raise ValueError("amax must have one entry per row")
+    xq = torch.empty((M, K), dtype=FP8, device=x.device)
+    sx = torch.empty((M,), dtype=torch.float32, device=x.device)
+    check(_lib.load().ms_quantize_rows_fp8_amax(ptr(x2), x2.stride(0), M, K, ptr(amax), ptr(xq), ptr(sx),
+                                                stream_ptr()), "ms_quantize_rows_fp8_amax")
+    return xq, sx
+
+
 def fp8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
              bias: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
     """y [M, N] fp16 = fp16((xq . wq^T) * sx[:, None] * sw[None, :]) (+ bias)."""

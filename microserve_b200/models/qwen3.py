@@ -36,6 +36,21 @@ from microserve_b200.utils import dist as tp
 from microserve_b200.utils.context import AttentionMode, get_context
 
 
+def tp_quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """FP8 rows of a row-parallel linear's input (the attention output for o_proj,
+    SiLU*mul for down_proj), which is sharded along K under tensor parallelism.
+    The reference scales each row by its amax over the FULL K
+    (microserve/layers/fp8_linear.py:20). By default each rank scales its shard
+    by the shard's own amax (no communication; equal to the reference at TP=1).
+    With exact activation scales (utils.dist.set_exact_act_scale) the ranks
+    all-reduce the row amax (max of M floats) first, so every code equals the
+    single-GPU code."""
+    if tp.tp_size() == 1 or not tp.exact_act_scale():
+        return kernels.quantize_rows_fp8(x)
+    amax = tp.all_reduce_max_(kernels.row_amax(x))
+    return kernels.quantize_rows_fp8_amax(x, amax)
+
+
 class Qwen3Attention(nn.Module):
     def __init__(self, hidden_size: int, num_heads: int, num_kv_heads: int, max_position: int,
                  head_dim: int | None = None, rms_norm_eps: float = 1e-6, qkv_bias: bool = False,
@@ -87,7 +102,7 @@ class Qwen3Attention(nn.Module):
             self.k_norm.weight if self.has_qk_norm else None, self.rms_norm_eps, ctx.slot_mapping,
             (attn.k_cache, attn.v_cache, attn.k_scale_cache, attn.v_scale_cache), want_kv=want_kv)
         o = attn.forward_cached(q, k, v)
-        oq, so = kernels.quantize_rows_fp8(o.view(-1, self.q_size))
+        oq, so = tp_quantize_rows(o.view(-1, self.q_size))
         return self.o_proj.forward_fp8(oq, so, reduce=partial_out is None, out=partial_out)
 
 
@@ -105,7 +120,11 @@ class Qwen3MLP(nn.Module):
     def forward_fp8(self, xq: torch.Tensor, sx: torch.Tensor, partial_out: torch.Tensor | None = None
                     ) -> torch.Tensor:
         gu = self.gate_up_proj.forward_fp8(xq, sx)
-        aq, sa = self.act_fn.forward_fp8(gu)
+        if tp.exact_act_scale():
+            a, _, _ = kernels.silu_mul(gu, want_fp16=True, want_fp8=False)
+            aq, sa = tp_quantize_rows(a)
+        else:
+            aq, sa = self.act_fn.forward_fp8(gu)
         return self.down_proj.forward_fp8(aq, sa, reduce=partial_out is None, out=partial_out)
 
 
@@ -151,14 +170,14 @@ class Qwen3DecoderLayer(nn.Module):
             xq, sx, _ = self.input_layernorm.forward_fp8(hidden_states)
             residual = hidden_states
         elif tpf is not None:
-            xq, sx = tpf.allreduce_norm_fp8(rows, residual, self.input_layernorm.weight, self.input_layernorm.eps, 0)
+            xq, sx = tpf.allreduce_norm_fp8(rows, residual, self.input_layernorm.weight, self.input_layernorm.eps)
         else:
             xq, sx, residual = self.input_layernorm.forward_fp8(hidden_states, residual)
         part = tpf.partial(rows) if tpf is not None else None
         h = self.self_attn.forward_fp8(positions, xq, sx, partial_out=part)
         if tpf is not None:
             xq, sx = tpf.allreduce_norm_fp8(rows, residual, self.post_attention_layernorm.weight,
-                                            self.post_attention_layernorm.eps, 1)
+                                            self.post_attention_layernorm.eps)
         else:
             xq, sx, residual = self.post_attention_layernorm.forward_fp8(h, residual)
         return self.mlp.forward_fp8(xq, sx, partial_out=part), residual

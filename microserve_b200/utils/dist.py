@@ -12,6 +12,7 @@ import torch.distributed as dist
 _GROUP = None
 _RANK = 0
 _SIZE = 1
+_EXACT_ACT_SCALE = False
 
 
 def init_tensor_parallel(group=None) -> None:
@@ -25,8 +26,20 @@ def init_tensor_parallel(group=None) -> None:
 
 
 def reset_tensor_parallel() -> None:
-    global _GROUP, _RANK, _SIZE
-    _GROUP, _RANK, _SIZE = None, 0, 1
+    global _GROUP, _RANK, _SIZE, _EXACT_ACT_SCALE
+    _GROUP, _RANK, _SIZE, _EXACT_ACT_SCALE = None, 0, 1, False
+
+
+def set_exact_act_scale(enable: bool) -> None:
+    """Row-parallel activation scales from the full row (an all-reduce max of one
+    float per row before each o_proj / down_proj quantisation) instead of the
+    local shard: FP8 codes identical to TP=1, one small collective more."""
+    global _EXACT_ACT_SCALE
+    _EXACT_ACT_SCALE = bool(enable)
+
+
+def exact_act_scale() -> bool:
+    return _EXACT_ACT_SCALE and _SIZE > 1
 
 
 def tp_rank() -> int:

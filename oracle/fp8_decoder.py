@@ -147,6 +147,25 @@ def decode_attention(q, k_cache, v_cache, k_scale, v_scale, seqlens, block_table
     return out.half()
 
 
+def decode_attention_grouped(q, k_cache, v_cache, k_scale, v_scale, seqlens, block_tables, sm_scale):
+    """decode_attention with the q heads of each kv head grouped instead of K/V copied
+    per q head (the same math, about twice as fast on the host cores; used where the
+    oracle is timed, pinned to decode_attention by tests/test_oracle_cpu.py)."""
+    B, Hq, D = q.shape
+    Hkv = k_cache.shape[2]
+    G = Hq // Hkv
+    out = torch.zeros(B, Hq, D, dtype=torch.float32)
+    for b in range(B):
+        L = int(seqlens[b])
+        if L == 0:
+            continue
+        kk = gather_kv(k_cache, k_scale, block_tables[b], L)
+        vv = gather_kv(v_cache, v_scale, block_tables[b], L)
+        s = torch.einsum("hgd,lhd->hgl", q[b].float().view(Hkv, G, D), kk) * sm_scale
+        out[b] = torch.einsum("hgl,lhd->hgd", s.softmax(-1), vv).reshape(Hq, D)
+    return out.half()
+
+
 def chunk_prefill_attention(q, k_cache, v_cache, k_scale, v_scale, table, prefix_len, sm_scale):
     """Single-sequence causal chunk attention over the cache
     (tests/test_fp8_kv_attention.py:96-105; kernel microserve/layers/fp8_chunk_prefill_attention.py:8-67)."""
@@ -189,10 +208,12 @@ class LayerWeights:
 
 
 def decoder_layer(lw: LayerWeights, positions, hidden, residual, *, Hq, Hkv, D, eps, cos_cache, sin_cache,
-                  mode: str, caches, slots, seqlens=None, block_tables=None, cu=None, prefix_len=None):
+                  mode: str, caches, slots, seqlens=None, block_tables=None, cu=None, prefix_len=None,
+                  grouped_attention: bool = False):
     """Qwen3DecoderLayer.forward with FP8 linears and the FP8 KV cache
     (microserve/models/qwen3.py:42-54,65-66,91-100; attention.py:36-61).
-    mode: "decode" | "prefill" | "chunk" (chunk: one sequence, block_tables[0], prefix_len)."""
+    mode: "decode" | "prefill" | "chunk" (chunk: one sequence, block_tables[0], prefix_len).
+    grouped_attention: decode attention through decode_attention_grouped (same math)."""
     if residual is None:
         h, residual = rmsnorm(hidden, lw.in_norm, eps), hidden
     else:
@@ -209,7 +230,8 @@ def decoder_layer(lw: LayerWeights, positions, hidden, residual, *, Hq, Hkv, D, 
     store_kv(k, v, kc, vc, ks, vs, slots)
     scale = D ** -0.5
     if mode == "decode":
-        o = decode_attention(q, kc, vc, ks, vs, seqlens, block_tables, scale)
+        attend = decode_attention_grouped if grouped_attention else decode_attention
+        o = attend(q, kc, vc, ks, vs, seqlens, block_tables, scale)
     elif mode == "prefill":
         o = varlen_prefill(q, k, v, cu, scale)
     elif mode == "chunk":

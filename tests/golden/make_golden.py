@@ -167,7 +167,9 @@ def scheduler_traces():
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
+    ref = Path(sys.argv[1])
     sys.path.insert(0, str(ref))
     torch.save(layer_goldens(), HERE / "layers_cpu.pt")
     with open(HERE / "scheduler_traces.json", "w") as f:

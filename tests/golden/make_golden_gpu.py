@@ -2,7 +2,8 @@
 kernels (its Triton kernels and its flash-attn call) on a B200.
 
 The reference package must be importable (installed offline into
-baseline/_ref); this script is run once on a GPU box:
+baseline/_ref with pip --no-index --no-deps --target baseline/_ref); this
+script is run once on a GPU box:
 
     PYTHONPATH=baseline/_ref python tests/golden/make_golden_gpu.py out.pt
 

@@ -82,6 +82,30 @@ def test_oracle_decode_attention_known_answer():
         assert torch.allclose(out[0, h].float(), (p[:, None] * vv).sum(0), atol=1e-3)
 
 
+def test_oracle_grouped_decode_attention_equals_the_loop():
+    """The grouped-head decode attention (used where the oracle is timed) computes
+    the same thing as the per-head restatement: paged, out-of-order blocks, ragged
+    lengths, an empty row, four q heads per kv head."""
+    g = torch.Generator().manual_seed(3)
+    Hq, Hkv, D, bs = 8, 2, 128, 256
+    lens = [300, 0, 17, 520]
+    nblk = [(L + bs - 1) // bs or 1 for L in lens]
+    perm = torch.randperm(sum(nblk), generator=g).tolist()
+    tables, o = [], 0
+    for n in nblk:
+        tables.append(perm[o:o + n])
+        o += n
+    kc = torch.randint(0, 120, (sum(nblk), bs, Hkv, D), dtype=torch.uint8, generator=g).view(torch.float8_e4m3fn)
+    vc = torch.randint(0, 120, (sum(nblk), bs, Hkv, D), dtype=torch.uint8, generator=g).view(torch.float8_e4m3fn)
+    ks = torch.rand(sum(nblk), bs, Hkv, generator=g) * 1e-2
+    vs = torch.rand(sum(nblk), bs, Hkv, generator=g) * 1e-2
+    q = torch.randn(len(lens), Hq, D, generator=g).half()
+    args = (q, kc, vc, ks, vs, torch.tensor(lens), O.block_table_rows(tables), D ** -0.5)
+    a, b = O.decode_attention(*args), O.decode_attention_grouped(*args)
+    assert (b[1] == 0).all()
+    assert (a.float() - b.float()).abs().max().item() < 1e-3
+
+
 # ------------------------------------------------------------------ scheduler / block manager
 def _replay(trace):
     from microserve_b200.engine.scheduler import Scheduler

@@ -1,19 +1,26 @@
-"""The fused tensor-parallel op (ms_tp_allreduce_rmsnorm_fp8) on two GPUs against
-the single-process composition it replaces: all-reduce of the row-parallel
-partial outputs (fp16 result), then ms_rmsnorm's residual add, RMSNorm and FP8
-row quantisation (itself tested against the oracle in test_kernels_gpu.py).
-The owned residual rows (sum in rank order, fp16 add) are bit-exact. The fused
-op reduces a row's sum of squares in a different order than ms_rmsnorm (one
-512-thread CTA per row vs ms_rmsnorm's row groups), so a normalised element
-can differ by one fp16 ulp: the normalised rows are held to the reference
-RMSNorm tolerance with nearly every element identical, and nearly every FP8
-code and scale identical. Skipped when fewer than two GPUs are visible."""
+"""Tensor parallelism on two GPUs.
+
+* The fused op (ms_tp_allreduce_rmsnorm_fp8) against the oracle and against
+  the single-GPU kernel it replaces: the owned residual rows equal the
+  oracle's all-reduce (fp32 sum of the parts in rank order, rounded to fp16)
+  plus the residual, bit for bit; the normalised rows are within the
+  reference RMSNorm tolerance of the oracle; and codes, scales and fp16 rows
+  are bit-identical to ms_rmsnorm applied to the summed rows (both kernels
+  share the canonical sum of squares of csrc/rowops.cuh).
+* Exact activation scales: each rank quantises its K shard of a row with the
+  all-reduced row amax, and its codes equal the single-GPU codes of that
+  slice of the full row, bit for bit.
+* The model: fused-collective prefill logits against the same weights through
+  NCCL all-reduce + RMSNorm.
+Skipped when fewer than two GPUs are visible."""
 import os
 
 import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+
+from oracle import fp8_decoder as O
 
 pytestmark = pytest.mark.gpu
 
@@ -28,48 +35,67 @@ def _case(seed, rows, world):
     return parts, residual, weight
 
 
-def _expected(parts, residual, weight):
-    """The composition the op replaces, with this library's own row kernels."""
-    from microserve_b200 import kernels
-    total = torch.stack([p.float() for p in parts]).sum(0).half()  # the all-reduce result (fp16)
-    y, q, s, r = kernels.rmsnorm(total.cuda(), weight.cuda(), 1e-6, residual.cuda(), want_fp16=True, want_fp8=True)
-    return q.cpu(), s.cpu(), r.cpu(), y.cpu()
+def _init_nccl(rank, world, port):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
 
 
-def _worker(rank, world, init_file, errq):
+def _op_worker(rank, world, port, errq):
     try:
-        torch.cuda.set_device(rank)
-        dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
-        from microserve_b200 import _lib
+        _init_nccl(rank, world, port)
+        from microserve_b200 import _lib, kernels
         from microserve_b200.utils import dist as tp
         from microserve_b200.utils.tp_fused import TpFused
         tp.init_tensor_parallel()
         f = TpFused(64, H, torch.device("cuda", rank))
-        for it, rows in enumerate((64, 37, 64, 1)):
+        # several calls in a row: row counts change, fp16 and FP8 outputs alternate, and
+        # the receive slots of both epoch parities are used and cleared
+        for it, (rows, want_h) in enumerate(((64, False), (37, False), (64, True), (1, False), (64, False),
+                                             (63, True), (2, False), (64, False))):
             parts, residual, weight = _case(100 + it, rows, world)
             f.partial(rows).copy_(parts[rank].cuda())
-            torch.cuda.synchronize()
-            dist.barrier()  # every rank's partial is written (the op's own barrier covers the GEMM order)
             res = residual.cuda()
-            if it == 3:
+            if want_h:
                 h = f.allreduce_norm_fp16(rows, res, weight.cuda(), 1e-6)
             else:
-                q, s = f.allreduce_norm_fp8(rows, res, weight.cuda(), 1e-6, it % 2)
+                q, s = f.allreduce_norm_fp8(rows, res, weight.cuda(), 1e-6)
             torch.cuda.synchronize()
-            eq, es, er, ey = _expected(parts, residual, weight)
+            # oracle: the all-reduce (fp32 sum in rank order -> fp16), the residual add, RMSNorm
+            total = torch.stack([p.float() for p in parts]).sum(0).half()
+            o_y, o_res = O.rmsnorm(total, weight, 1e-6, residual)
+            o_q, o_s = O.quantize_rows(o_y)
+            # the single-GPU kernel on the same summed rows
+            ky, kq, ks, kr = kernels.rmsnorm(total.cuda(), weight.cuda(), 1e-6, residual.cuda(), want_fp16=True,
+                                             want_fp8=True)
             R = (rows + world - 1) // world
             own = slice(rank * R, min(rows, (rank + 1) * R))
-            assert torch.equal(res.cpu()[own], er[own]), f"residual rows, call {it}"
-            if it == 3:
-                torch.testing.assert_close(h.cpu(), ey, atol=1e-3, rtol=1e-3)
-                assert (h.cpu() == ey).float().mean().item() > 0.99, "fp16 rows"
+            assert torch.equal(res.cpu()[own], o_res[own]), f"residual rows vs oracle, call {it}"
+            assert torch.equal(kr.cpu()[own], o_res[own])
+            if want_h:
+                torch.testing.assert_close(h.cpu(), o_y, atol=1e-3, rtol=1e-3)
+                assert torch.equal(h.cpu(), ky.cpu()), f"fp16 rows vs ms_rmsnorm, call {it}"
             else:
-                sc = s.cpu()
-                assert ((sc - es).abs() <= 2e-3 * es.abs()).all(), f"scales, call {it}"
-                assert (sc == es).float().mean().item() > 0.9, f"scales, call {it}"
-                same = (q.cpu().view(torch.uint8) == eq.view(torch.uint8)).float().mean().item()
-                assert same > 0.995, f"codes, call {it}: {same}"
+                assert torch.equal(s.cpu(), ks.cpu()), f"scales vs ms_rmsnorm, call {it}"
+                assert torch.equal(q.cpu().view(torch.uint8), kq.cpu().view(torch.uint8)), f"codes, call {it}"
+                assert ((s.cpu() - o_s).abs() <= 2e-3 * o_s).all(), f"scales vs oracle, call {it}"
+                same = (q.cpu().view(torch.uint8) == o_q.view(torch.uint8)).float().mean().item()
+                assert same > 0.99, f"codes vs oracle, call {it}: {same}"
         assert _lib.device_status() == 0
+
+        # exact activation scales: shard k of a full row quantised with the global row amax
+        g = torch.Generator().manual_seed(5)
+        full = (torch.randn(40, 2 * 2048, generator=g) * torch.rand(40, 1, generator=g) * 4).half()
+        K = full.shape[1] // world
+        shard = full[:, rank * K:(rank + 1) * K].contiguous().cuda()
+        amax = tp.all_reduce_max_(kernels.row_amax(shard))
+        sq, ss = kernels.quantize_rows_fp8_amax(shard, amax)
+        fq, fs = kernels.quantize_rows_fp8(full.cuda())
+        torch.cuda.synchronize()
+        assert torch.equal(ss.cpu(), fs.cpu())
+        assert torch.equal(sq.cpu().view(torch.uint8), fq.cpu()[:, rank * K:(rank + 1) * K].view(torch.uint8))
         dist.barrier()
         f.close()
         dist.destroy_process_group()
@@ -80,15 +106,22 @@ def _worker(rank, world, init_file, errq):
     os._exit(0)
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_allreduce_rmsnorm_fp8_two_gpus(tmp_path):
+def _free_port():
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(target, world, timeout):
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, str(tmp_path / "pg"), errq)) for r in range(2)]
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, errq)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=300)
+        p.join(timeout=timeout)
     errs = []
     while not errq.empty():
         errs.append(errq.get())
@@ -99,13 +132,14 @@ def test_fused_allreduce_rmsnorm_fp8_two_gpus(tmp_path):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
 
 
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_allreduce_rmsnorm_fp8_two_gpus():
+    _run(_op_worker, 2, 300)
+
+
 def _model_worker(rank, world, port, errq):
     try:
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
-        torch.cuda.set_device(rank)
-        import datetime
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", rank))
+        _init_nccl(rank, world, port)
         import numpy as np
         from microserve_b200 import _lib
         from microserve_b200.Config import Config
@@ -163,22 +197,4 @@ def test_tp2_model_fused_collective_matches_nccl():
     of test_model_gpu.py): logits agree to a relative L2 of 5e-2 with > 85 %
     identical greedy tokens; a wrong row ownership or a missed peer row gives
     relative errors of order 1."""
-    import socket
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        port = s.getsockname()[1]
-    ctx = mp.get_context("spawn")
-    errq = ctx.Queue()
-    procs = [ctx.Process(target=_model_worker, args=(r, 2, port, errq)) for r in range(2)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=400)
-    errs = []
-    while not errq.empty():
-        errs.append(errq.get())
-    for p in procs:
-        if p.is_alive():
-            p.kill()
-    assert not errs, "\n".join(errs)
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    _run(_model_worker, 2, 400)

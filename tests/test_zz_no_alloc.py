@@ -75,19 +75,21 @@ def test_noalloc_decode_matches_workspace_entry_point_twice():
 
 
 def test_noalloc_rejects_batches_beyond_its_buffer():
-    from microserve_b200 import _lib
+    from microserve_b200 import _lib, kernels
     lib = _lib.load()
     dev = "cuda"
-    # 73 sequences x 8 kv heads = 584 CTAs: a 2-way context split, 73 x 64 x 2 partial rows of
-    # (128 + 2) floats = 4.9 MB, more than the 4 MiB built-in buffer
-    B, Hq, Hkv = 73, 64, 8
+    Hq, Hkv, nblk = 64, 8, 64
+    # the first batch size (on this device's SM count) whose context split needs
+    # more scratch than the 4 MiB built-in buffer holds
+    B = next((b for b in range(1, 4096) if kernels.decode_workspace_bytes(b, Hq, Hkv, nblk, BS) > 4 << 20), None)
+    assert B is not None
     q = torch.zeros(B, Hq, D, dtype=torch.float16, device=dev)
     kc = torch.zeros(1, BS, Hkv, D, dtype=torch.float8_e4m3fn, device=dev)
     ks = torch.ones(1, BS, Hkv, device=dev)
     lens = torch.zeros(B, dtype=torch.int32, device=dev)
-    bt = torch.zeros(B, 4, dtype=torch.int32, device=dev)
+    bt = torch.zeros(B, nblk, dtype=torch.int32, device=dev)
     rc = lib.ms_paged_decode_fp8_noalloc(q.data_ptr(), kc.data_ptr(), kc.data_ptr(), ks.data_ptr(), ks.data_ptr(),
-                                         lens.data_ptr(), bt.data_ptr(), q.data_ptr(), B, Hq, Hkv, D, BS, 4,
+                                         lens.data_ptr(), bt.data_ptr(), q.data_ptr(), B, Hq, Hkv, D, BS, nblk,
                                          ctypes.c_float(1.0), 0)
     assert rc == _lib.MS_ERR_UNSUPPORTED
     assert b"built-in buffer" in lib.ms_last_error()
