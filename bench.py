@@ -376,6 +376,27 @@ def kernel_rooflines(engine, batch, step_idx, hbm_peak):
             t = time_kernel(lambda: tpf.allreduce_norm_fp8(B, res_rows, w, eps))
             res["tp_allreduce_rmsnorm_fp8"] = dict(seconds=t, bytes=(world - 1) * R * (2 * H + H + 4), per_layer=2,
                                                    bound="nvlink", peak_gbs=NVLINK_PEER_GBS)
+        if tpf is not None:
+            # o_proj as the decode step runs it: the row-parallel GEMM pushing its output rows
+            # to their owners (overlapping the transfer with the GEMM) + the op that reduces,
+            # normalises and gathers. Communication hidden = 1 - exposed / standalone, with
+            # exposed = pair - (local GEMM + the norm alone) and standalone = op - norm alone.
+            o = layer.self_attn.o_proj
+            xo = torch.randn(B, o.in_features, device=dev, generator=g).half()
+            oq, so = kernels.quantize_rows_fp8(xo)
+            sync_all()
+
+            def pair():
+                tpf.rowpar_gemm(oq, so, o.weight_fp8, o.weight_scale)
+                tpf.allreduce_norm_fp8(B, res_rows, w, eps, pushed=True)
+            t = time_kernel(pair)
+            op_t = res["tp_allreduce_rmsnorm_fp8"]["seconds"]
+            norm_t, gemm_t = res["rmsnorm_fp8"]["seconds"], res["o_proj"]["seconds"]
+            exposed = max(0.0, t - gemm_t - norm_t)
+            res["tp_o_proj_pushed_pair"] = dict(
+                seconds=t, bytes=(world - 1) * R * (2 * H + H + 4), per_layer=1, bound="nvlink",
+                peak_gbs=NVLINK_PEER_GBS,
+                comm_hidden_frac=round(1.0 - min(1.0, exposed / max(op_t - norm_t, 1e-9)), 3))
         xr = torch.randn(B, H, device=dev, generator=g).half()
         sync_all()
         t = time_kernel(lambda: torch.distributed.all_reduce(xr, group=tp.tp_group()))
@@ -781,6 +802,74 @@ def reference_kernels():
     return fp8_decode_attention, _fp8_mm
 
 
+@torch.inference_mode()
+def run_tp_rowpar_sweep(args):
+    """BASELINE config 5, the fused row-parallel op under torchrun: for each M, the
+    row-parallel FP8 GEMM with N = hidden, K = intermediate / TP (down_proj of the
+    --model's shapes; 32B: N = 5120, K = 25600 / TP) pushing its output rows to their
+    owners + the all-reduce / residual / RMSNorm / FP8 op, against this rank's GEMM
+    writing locally + NCCL all-reduce + the RMSNorm/FP8 kernel. bf16/fp16 activations
+    N(0, 1). Device time per call (CUDA graph of 20 calls, max over ranks); NVLink
+    bytes each rank sends per call: its partial rows to their owners and its codes to
+    every peer."""
+    import datetime
+    from microserve_b200 import _lib, kernels
+    from microserve_b200.utils import dist as tp
+    from microserve_b200.utils.tp_fused import TpFused
+    rank, world, local = (int(os.environ.get(k, d)) for k, d in (("RANK", "0"), ("WORLD_SIZE", "1"),
+                                                                   ("LOCAL_RANK", "0")))
+    torch.cuda.set_device(local)
+    if world < 2:
+        print(json.dumps({"kernel": "tp_rowpar", "unavailable": "needs torchrun with 2..8 ranks"}), flush=True)
+        return
+    torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                         device_id=torch.device("cuda", local))
+    tp.init_tensor_parallel()
+    _lib.load().ms_set_pdl(1)
+    m = MODELS[args.model]
+    H, K = m["hidden"], m["inter"] // world
+    Ms = [int(x) for x in (args.rows or "1,8,64,256,1024,4096,8192").split(",")]
+    dev = torch.device("cuda", local)
+    f = TpFused(max(Ms), H, dev)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    wq, sw = kernels.quantize_rows_fp8((torch.randn(H, K, device=dev, generator=g) * 0.02).half())
+    nw = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).half()
+    for M in Ms:
+        xq, sx = kernels.quantize_rows_fp8(torch.randn(M, K, device=dev, generator=g).half())
+        res = torch.randn(M, H, device=dev, generator=g).half()
+        y = torch.empty(M, H, device=dev, dtype=torch.float16)
+
+        def fused():
+            f.rowpar_gemm(xq, sx, wq, sw)
+            f.allreduce_norm_fp8(M, res, nw, 1e-6, pushed=True)
+
+        def baseline():
+            kernels.fp8_gemm(xq, sx, wq, sw, out=y)
+            torch.distributed.all_reduce(y, group=tp.tp_group())
+            kernels.rmsnorm(y, nw, 1e-6, res, want_fp16=False, want_fp8=True)
+        sync_all()
+        t_fused = max_over_ranks(time_kernel(fused))
+        sync_all()
+        t_base = max_over_ranks(time_kernel(baseline))
+        sync_all()
+        t_gemm = max_over_ranks(time_kernel(lambda: kernels.fp8_gemm(xq, sx, wq, sw, out=y)))
+        R = (M + world - 1) // world
+        sent = (world - 1) * R * (2 * H + H + 4)
+        flops = 2 * M * H * K
+        if rank == 0:
+            print(json.dumps({"kernel": "tp_rowpar_gemm_allreduce_rmsnorm_fp8", "model": args.model, "tp": world,
+                              "M": M, "N": H, "K": K, "fused_us": round(t_fused * 1e6, 2),
+                              "gemm_nccl_rmsnorm_us": round(t_base * 1e6, 2), "gemm_alone_us": round(t_gemm * 1e6, 2),
+                              "speedup": round(t_base / t_fused, 3),
+                              "nvlink_sent_bytes": sent, "nvlink_GBps_if_comm_only": round(sent / t_fused / 1e9, 1),
+                              "TFLOPs": round(flops / t_fused / 1e12, 1)}), flush=True)
+    status = _lib.device_status()
+    if rank == 0:
+        print(json.dumps({"kernel": "tp_rowpar", "device_status": status}), flush=True)
+    f.close()
+    shutdown_distributed()
+
+
 def run_kernel(args):
     """One kernel on synthetic inputs of a Qwen3 layer's shapes, timed with CUDA events
     (used for the kernel sweeps of BASELINE config 5 and for ncu captures). One JSON line
@@ -888,14 +977,18 @@ def main():
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch the library's kernels without programmatic dependent launch")
     ap.add_argument("--kv-blocks", type=int, default=0, help="KV-cache blocks (0: size from free memory)")
-    ap.add_argument("--kernel", choices=["decode_attention", "gemm"], default=None,
+    ap.add_argument("--rows", type=str, default="",
+                    help="--kernel tp_rowpar: token counts M, comma list (default 1..8192)")
+    ap.add_argument("--kernel", choices=["decode_attention", "gemm", "tp_rowpar"], default=None,
                     help="time one kernel on synthetic inputs (sweeps / profiling) instead of the model")
     ap.add_argument("--ctx", type=str, default="832", help="--kernel decode_attention: context lengths, comma list")
     ap.add_argument("--shapes", type=str, default="",
                     help="--kernel gemm: M:N:K comma list (default: the 8B layer's four linears at M=--batch)")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
-    if args.kernel is not None:
+    if args.kernel == "tp_rowpar":
+        run_tp_rowpar_sweep(args)
+    elif args.kernel is not None:
         run_kernel(args)  # --impl reference: the reference's own Triton kernel on the same inputs
     elif args.impl == "reference":
         run_reference(args)

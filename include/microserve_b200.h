@@ -198,12 +198,13 @@ int ms_ipc_close(void* base);
 
 /* Byte offsets inside one rank's communication buffer for the fused op below
  * (world ranks, hidden size H, at most max_rows rows per call):
- *   offsets[0] partial   [max_rows, H] fp16  this rank's row-parallel output (the GEMM's out)
- *   offsets[1] recv      receive slots peers write (internal)
- *   offsets[2] gather_q  [max_rows, H] e4m3  every rank's normalised rows, FP8 codes
- *   offsets[3] gather_s  [max_rows] fp32     their scales
- *   offsets[4] gather_h  [max_rows, H] fp16  normalised fp16 rows (want_fp16 calls)
- *   offsets[5] control words, offsets[6] total bytes.
+ *   offsets[0] partial  [max_rows, H] fp16  this rank's row-parallel output, when
+ *                                           the GEMM does not push its tiles itself
+ *   offsets[1] out_q    [max_rows, H] e4m3  the normalised rows of the last call (FP8 codes)
+ *   offsets[2] out_s    [max_rows] fp32     their scales
+ *   offsets[3] out_h    [max_rows, H] fp16  the normalised rows of the last want_fp16 call
+ *   offsets[4] total bytes.
+ * The rest of the buffer holds the receive slots peers write (internal).
  * No reference counterpart (plumbing of the op below). */
 int ms_tp_layout(int world, int64_t hidden, int64_t max_rows, int64_t* offsets);
 
@@ -216,24 +217,41 @@ int ms_tp_buffer_init(void* base, int world, int64_t hidden, int64_t max_rows, v
 /* Row-parallel all-reduce + residual add + RMSNorm + FP8 row quantisation, one
  * kernel per rank. bases[p] = rank p's communication buffer as mapped in this
  * process (CUDA IPC; bases[rank] is the local one). The rank's row-parallel
- * output [M, H] fp16 is read from its partial area. With R = ceil(M / world),
- * rank r owns rows [r R, (r + 1) R): it sums those rows of every rank's output
- * in rank order (fp32, rounded to fp16 once), adds its residual rows (updated
- * in place, fp16), normalises them (weight [H] fp16, eps) and writes codes +
- * scales (and, with want_fp16, the fp16 rows) into every rank's gather area;
- * the call returns (on the GPU) once every rank's rows are in this rank's
- * gather area. Rows of the residual that the rank does not own are neither
- * read nor written. Readiness is carried by the data (no flags); every wait is
- * bounded (ms_set_wait_limit) and a wait that runs out records status 2 (peer
- * timeout, ms_get_device_status), after which the buffers of the whole group
- * must be re-initialised. Every rank makes the same sequence of calls.
+ * output [M, H] fp16 is read from its partial area, or - with pushed != 0 - is
+ * already in the receive slots because ms_fp8_gemm_rowpar wrote it there. With
+ * R = ceil(M / world), rank r owns rows [r R, (r + 1) R): it sums those rows of
+ * every rank's output in rank order (fp32, rounded to fp16 once), adds its
+ * residual rows (updated in place, fp16), normalises them (weight [H] fp16, eps)
+ * and sends codes + scales (with want_fp16: fp16 rows) to every rank; on the
+ * GPU the call ends once all M rows are in this rank's out area. Rows of the
+ * residual that the rank does not own are neither read nor written. Readiness
+ * is carried by the data (no flags); every wait is bounded (ms_set_wait_limit)
+ * and a wait that runs out records status 2 (peer timeout, ms_get_device_status),
+ * after which the buffers of the whole group must be re-initialised. Every rank
+ * makes the same sequence of calls with the same M.
  * Replaces RowParallelLinear's dist.all_reduce (microserve/layers/linear.py:70-77)
  * + the add/RMSNorm that follows (layers/layernorm.py:22-42) + the next FP8
  * activation quantisation (layers/fp8_linear.py:14-23).
  * world <= 8, H % 16 == 0, H <= 16384, 0 <= M <= max_rows. */
 int ms_tp_allreduce_rmsnorm_fp8(void* const* bases, int rank, int world, int64_t hidden, int64_t max_rows,
-                                void* residual, const void* weight, int64_t M, float eps, int want_fp16,
+                                void* residual, const void* weight, int64_t M, float eps, int want_fp16, int pushed,
                                 void* stream);
+
+/* The row-parallel FP8 GEMM of tensor parallelism (o_proj, down_proj) with its
+ * output pushed to the ranks that own the rows: Y = fp16((Xq . Wq^T) * sx * sw)
+ * as ms_fp8_gemm (xq [M, K], wq [N, K] this rank's K shard, N = the hidden size
+ * of the buffers), except that each output row m is written - by the GEMM's
+ * epilogue, tile by tile, as tiles finish - into the receive slot of rank
+ * m / ceil(M / world) in that rank's communication buffer (bases as for
+ * ms_tp_allreduce_rmsnorm_fp8), so the transfer overlaps the GEMM. Follow it
+ * with ms_tp_allreduce_rmsnorm_fp8(..., pushed = 1) on the same stream.
+ * workspace: ms_fp8_gemm_workspace_size(M, N, K) bytes. Replaces the GEMM of
+ * RowParallelLinear (microserve/layers/linear.py:70-77; F.linear, or
+ * FP8DynamicLinear.forward when quantised, layers/fp8_linear.py:64-80) and the
+ * transfer half of its dist.all_reduce. */
+int ms_fp8_gemm_rowpar(const void* xq, const float* sx, const void* wq, const float* sw, int64_t M, int64_t N,
+                       int64_t K, void* workspace, size_t workspace_bytes, void* const* bases, int rank, int world,
+                       int64_t max_rows, void* stream);
 
 /* Upper bound, in nanoseconds, of every in-kernel wait on the current device
  * (peer data, pipeline barriers); default 4e9. A wait that runs out records a

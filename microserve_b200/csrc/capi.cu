@@ -11,6 +11,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tp_rows.cuh"
 
 namespace {
 
@@ -313,7 +314,7 @@ int ms_tp_layout(int world, int64_t hidden, int64_t max_rows, int64_t* offsets) 
   if (world < 1 || world > 8 || hidden <= 0 || max_rows <= 0 || !offsets)
     return fail(MS_ERR_INVALID, "ms_tp_layout: bad arguments");
   const ms::TpLayout l = ms::tp_layout(world, hidden, max_rows);
-  const int64_t o[7] = {l.partial, l.recv, l.gq, l.gs, l.gh, l.ctrl, l.total};
+  const int64_t o[5] = {l.partial, l.outq, l.outs, l.outh, l.total};
   memcpy(offsets, o, sizeof(o));
   return MS_OK;
 }
@@ -326,7 +327,7 @@ int ms_tp_buffer_init(void* base, int world, int64_t hidden, int64_t max_rows, v
 }
 
 int ms_tp_allreduce_rmsnorm_fp8(void* const* bases, int rank, int world, int64_t hidden, int64_t max_rows,
-                                void* residual, const void* weight, int64_t M, float eps, int want_fp16,
+                                void* residual, const void* weight, int64_t M, float eps, int want_fp16, int pushed,
                                 void* stream) {
   if (world < 1 || world > 8 || rank < 0 || rank >= world || M < 0 || max_rows <= 0 || M > max_rows ||
       max_rows > INT32_MAX || hidden <= 0)
@@ -343,8 +344,31 @@ int ms_tp_allreduce_rmsnorm_fp8(void* const* bases, int rank, int world, int64_t
   if (((uintptr_t)residual & 15) != 0 || ((uintptr_t)weight & 15) != 0)
     return fail(MS_ERR_INVALID, "ms_tp_allreduce_rmsnorm_fp8: residual/weight not 16-byte aligned");
   return check_cuda(ms::launch_tp_allreduce_rmsnorm_fp8(bases, rank, world, hidden, max_rows, residual, weight,
-                                                        (int)M, eps, want_fp16, num_sms(), S(stream)),
+                                                        (int)M, eps, want_fp16, pushed, num_sms(), S(stream)),
                     "ms_tp_allreduce_rmsnorm_fp8");
+}
+
+int ms_fp8_gemm_rowpar(const void* xq, const float* sx, const void* wq, const float* sw, int64_t M, int64_t N,
+                       int64_t K, void* workspace, size_t workspace_bytes, void* const* bases, int rank, int world,
+                       int64_t max_rows, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0 || M > max_rows || max_rows > INT32_MAX || N > 16384 || K > INT32_MAX ||
+      world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(MS_ERR_INVALID, "ms_fp8_gemm_rowpar: bad sizes M=%lld N=%lld K=%lld rank=%d world=%d", (long long)M,
+                (long long)N, (long long)K, rank, world);
+  if (M == 0) return MS_OK;
+  if (N % 16 != 0 || K % 16 != 0)
+    return fail(MS_ERR_UNSUPPORTED, "ms_fp8_gemm_rowpar: N and K must be multiples of 16");
+  if (!xq || !sx || !wq || !sw || !bases) return fail(MS_ERR_INVALID, "ms_fp8_gemm_rowpar: null pointer");
+  for (int p = 0; p < world; ++p)
+    if (!bases[p] || ((uintptr_t)bases[p] & 255) != 0)
+      return fail(MS_ERR_INVALID, "ms_fp8_gemm_rowpar: buffer of rank %d null or not 256-byte aligned", p);
+  const size_t need = ms::gemm_workspace_bytes((int)M, (int)N, (int)K, num_sms());
+  if (workspace_bytes < need || (need > 0 && workspace == nullptr))
+    return fail(MS_ERR_WORKSPACE, "ms_fp8_gemm_rowpar: workspace %zu < %zu bytes", workspace_bytes, need);
+  const ms::TpRows rp = ms::tp_rows_args(bases, rank, world, N, max_rows, (int)M);
+  return check_cuda(ms::launch_fp8_gemm(xq, sx, wq, sw, nullptr, nullptr, (int)M, (int)N, (int)K, workspace,
+                                        workspace_bytes, num_sms(), S(stream), &rp),
+                    "ms_fp8_gemm_rowpar");
 }
 
 int ms_set_wait_limit(uint64_t ns) {

@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tp_rows.cuh"
 
 namespace ms {
 namespace {
@@ -57,6 +58,13 @@ struct GemmArgs {
   float* ws;   // [G][BN][kBM] fp32 partial tiles (stream-K fixup)
   int* flags;  // [G] partial-ready flags; zero before and after every launch
   int tma_y;   // 1: the output tensor map is valid (N % 8 == 0, y 16-byte aligned)
+  // Row-parallel push (tensor parallelism, rp_R > 0): instead of y, output row m
+  // goes to rank m / rp_R's receive slot [b][rp_rank][m mod rp_R] (b = the parity
+  // of the epoch word *rp_ctrl), over NVLink for the other ranks (tp_rows.cuh).
+  __half* rp_recv[kTpMaxWorld];
+  const int* rp_ctrl;
+  int64_t rp_half, rp_src;  // elements of one parity set / of one source's slots
+  int rp_R, rp_rank;
 };
 
 // BN: token columns per tile (MMA N). CH: 128-byte K chunks per pipeline stage.
@@ -72,10 +80,11 @@ struct Cfg {
   static constexpr int kAccCols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));  // TMEM columns
   static constexpr int kTmemCols = 2 * kAccCols;  // two accumulators (double buffer)
   static constexpr int kSxBytes = 2 * BN * 4;     // token scales of the current tile, double-buffered
+  static constexpr int kRowsBytes = 2 * BN * 8;   // row-parallel push: destination of each token row
   static constexpr int kBarBytes = 256;
-  static constexpr int kFit = (227 * 1024 - 1024 - kBarBytes - kSxBytes) / kStageBytes;
+  static constexpr int kFit = (227 * 1024 - 1024 - kBarBytes - kSxBytes - kRowsBytes) / kStageBytes;
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + kBarBytes + kSxBytes;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + kBarBytes + kSxBytes + kRowsBytes;
   // tcgen05 instruction descriptor: D=f32, A=B=e4m3, both K-major, N=BN, M=128.
   static constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
   static_assert(kStages >= 2, "shared memory budget");
@@ -122,12 +131,23 @@ __device__ __forceinline__ void tma_store_2d_wait(const CUtensorMap* map, uint32
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// Row-parallel destination of output row m (rank m / R's receive slot for this rank).
+__device__ __forceinline__ __half* rp_row(const GemmArgs& a, int m, int b) {
+  const int owner = m / a.rp_R;
+  return a.rp_recv[owner] + (int64_t)b * a.rp_half + a.rp_rank * a.rp_src + (int64_t)(m - owner * a.rp_R) * a.N;
+}
+// A pushed value never has the receive slots' "not yet written" pattern (0xFFFF, a NaN).
+__device__ __forceinline__ __half rp_out(__half h) {
+  return __half_as_ushort(h) == 0xFFFFu ? __ushort_as_half((unsigned short)0x7FFFu) : h;
+}
+
 // Output of 16 token columns of one weight row n: y = fp16(fp16(v * sx * sw[n]) + bias[n]).
 // With `stage` the values go to a shared-memory tile [tokens][128 rows] fp16 (the
 // CTA then writes the tile with one bulk tensor store); without, straight to y
 // with one 2-byte store per token (64 bytes per warp instruction).
 __device__ __forceinline__ void out16(const GemmArgs& args, const float* v, const float* sx, float swn, float bn,
-                                      int m0, int c0, int cols, int n, __half* stage, int row) {
+                                      int m0, int c0, int cols, int n, __half* stage, int row,
+                                      __half* const* rows = nullptr) {
   const float4* sxv = reinterpret_cast<const float4*>(sx + c0);
   float sc[16];
 #pragma unroll
@@ -151,6 +171,12 @@ __device__ __forceinline__ void out16(const GemmArgs& args, const float* v, cons
     return;
   }
   if (n >= args.N) return;
+  if (rows != nullptr) {  // row-parallel push: each token row to its owner's slot
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (c0 + j < cols) rows[c0 + j][n] = rp_out(r[j]);
+    return;
+  }
   const int64_t N = args.N;
   __half* yp = args.y + (int64_t)(m0 + c0) * N + n;
   if (c0 + 16 <= cols) {
@@ -276,7 +302,7 @@ template <int BN, int CH>
 __device__ __forceinline__ void split_epilogue(const GemmArgs& args, uint32_t acc, int64_t t, int m0, int cols, int n,
                                                bool n_ok, float swn, float bn, const float* sx, float* my_ws,
                                                unsigned char* smem, uint64_t* red_full, uint64_t* acc_empty, int et,
-                                               int row) {
+                                               int row, __half* const* rows) {
   using C = Cfg<BN, CH>;
   const int S = args.splits;
   for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -337,6 +363,12 @@ __device__ __forceinline__ void split_epilogue(const GemmArgs& args, uint32_t ac
 #pragma unroll
       for (int j = 0; j < 16; ++j) r[j] = __float2half_rn(__half2float(r[j]) + bn);
     }
+    if (rows != nullptr) {  // row-parallel push
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (c0 + j < cols) rows[c0 + j][n] = rp_out(r[j]);
+      continue;
+    }
     __half* yp = args.y + (int64_t)(m0 + c0) * args.N + n;
 #pragma unroll
     for (int j = 0; j < 16; ++j)
@@ -381,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* red_full = acc_empty + 2;       // split-K: partial slices landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_full + 1);
   float* s_sx = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes + C::kBarBytes);  // [2][BN]
+  __half** s_rows = reinterpret_cast<__half**>(smem + C::kStages * C::kStageBytes + C::kBarBytes + C::kSxBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
@@ -491,6 +524,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = threadIdx.x - 64;
     float* my_ws = args.ws + (int64_t)cta * BN * kBM;
     pdl_wait();  // token scales come from the preceding grid; the workspace may be in use until it ends
+    // row-parallel push: the receive-slot parity of this call (the epoch word is
+    // advanced by the tensor-parallel op that precedes this GEMM in the stream)
+    const int rp_b = args.rp_R > 0 ? (*reinterpret_cast<const volatile int*>(args.rp_ctrl) & 1) : 0;
     int seg = -1;
     SegIter it(args, cta);
     int64_t t;
@@ -506,7 +542,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       float swn = 0.f, bn = 0.f;
       if (owner || args.splits > 0) {
         // scales are inputs: fetch them while the tile is still accumulating
-        for (int j = et; j < cols; j += 128) s_sx[b * BN + j] = args.sx[m0 + j];
+        for (int j = et; j < cols; j += 128) {
+          s_sx[b * BN + j] = args.sx[m0 + j];
+          if (args.rp_R > 0) s_rows[b * BN + j] = rp_row(args, m0 + j, rp_b);
+        }
         swn = n_ok ? args.sw[n] : 0.f;
         bn = (n_ok && args.bias != nullptr) ? __half2float(args.bias[n]) : 0.f;
       }
@@ -516,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       if (args.splits > 0) {
         split_epilogue<BN, CH>(args, acc, t, m0, cols, n, n_ok, swn, bn, s_sx + b * BN, my_ws, smem, red_full,
-                               acc_empty + b, et, row);
+                               acc_empty + b, et, row, args.rp_R > 0 ? s_rows + b * BN : nullptr);
         continue;
       }
       if (!owner) {
@@ -584,7 +623,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        out16(args, v, s_sx + b * BN, swn, bn, m0, c0, cols, n, stage, row);
+        out16(args, v, s_sx + b * BN, swn, bn, m0, c0, cols, n, stage, row,
+              args.rp_R > 0 ? s_rows + b * BN : nullptr);
       }
       if (stage != nullptr) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staged tile -> the bulk store
@@ -1029,8 +1069,9 @@ size_t gemm_workspace_bytes(int M, int N, int K, int num_sms) {
 
 cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,
                             void* y, int M, int N, int K, void* workspace, size_t workspace_bytes, int num_sms,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, const TpRows* rp) {
   if (M == 0 || N == 0) return cudaSuccess;
+  if (rp != nullptr && (K % 16 != 0 || rp->H != N || rp->M != M)) return cudaErrorInvalidValue;
   if (K % 16 != 0) {
     dim3 grid((N + 127) / 128, M);
     return launch_kernel(fp8_gemm_simt_kernel, grid, dim3(128), 0, stream, (const uint8_t*)xq, (const uint8_t*)wq, M,
@@ -1041,10 +1082,12 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   if (!p.dp && (gemm_workspace_bytes(M, N, K, num_sms) > workspace_bytes || workspace == nullptr))
     return cudaErrorInvalidValue;
   CUtensorMap mw, mx, my;
-  // The bulk store of a CTA's last output tile needs 16-byte aligned rows of y.
-  const bool tma_y = N % 8 == 0 && ((uintptr_t)y & 15) == 0 && make_map(&my, y, M, N, bn, 0);
+  // The bulk store of a CTA's last output tile needs 16-byte aligned rows of y
+  // (and a local y: pushed rows leave through plain stores).
+  const bool tma_y = rp == nullptr && N % 8 == 0 && ((uintptr_t)y & 15) == 0 && make_map(&my, y, M, N, bn, 0);
   if (!tma_y) memset(&my, 0, sizeof(my));
   if (p.wide) {
+    if (rp != nullptr) return cudaErrorInvalidValue;  // row-parallel outputs are never that wide
     if (!make_map(&mw, wq, N, K, kWideRows, 1) || !make_map(&mx, xq, M, K, kWideBN, 1)) return cudaErrorInvalidValue;
     GemmArgs args = {};
     args.M = M;
@@ -1067,7 +1110,15 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
     return launch_kernel(fp8_gemm_wide_kernel, dim3(args.G), dim3(kThreads), kWideSmem, stream, mw, mx, my, args);
   }
   if (!make_map(&mw, wq, N, K, kBM, p.ch) || !make_map(&mx, xq, M, K, bn, p.ch)) return cudaErrorInvalidValue;
-  GemmArgs args;
+  GemmArgs args = {};
+  if (rp != nullptr) {
+    for (int r = 0; r < rp->world; ++r) args.rp_recv[r] = rp->recv[r];
+    args.rp_ctrl = rp->ctrl;
+    args.rp_half = rp->recv_half;
+    args.rp_src = rp->recv_src;
+    args.rp_R = rp->R;
+    args.rp_rank = rp->rank;
+  }
   args.M = M;
   args.N = N;
   args.K = K;

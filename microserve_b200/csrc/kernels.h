@@ -41,15 +41,17 @@ cudaError_t launch_prefill_attention(bool paged, const void* q, const void* k16,
                                      int head_dim, int block_size, int max_blocks, float softmax_scale,
                                      cudaStream_t stream);
 
-// One rank's communication buffer for the fused tensor-parallel op: byte offsets.
+// One rank's communication buffer for the fused tensor-parallel op: byte offsets
+// (peers write [recv, ctrl); outq/outs/outh are the normalised rows this rank's
+// next op reads).
 struct TpLayout {
-  int64_t partial, recv, gq, gs, gh, ctrl, total;
+  int64_t partial, recv, grq, grs, grh, ctrl, outq, outs, outh, total;
 };
 TpLayout tp_layout(int world, int64_t H, int64_t max_rows);
 cudaError_t launch_tp_buffer_init(void* base, int world, int64_t H, int64_t max_rows, cudaStream_t stream);
 cudaError_t launch_tp_allreduce_rmsnorm_fp8(void* const* bases, int rank, int world, int64_t H, int64_t max_rows,
                                             void* residual, const void* weight, int M, float eps, int want_h,
-                                            int num_sms, cudaStream_t stream);
+                                            int pushed, int num_sms, cudaStream_t stream);
 
 size_t argmax_workspace_bytes(int64_t M);
 cudaError_t launch_argmax_rows(const void* x, int64_t M, int V, int64_t ldx, int64_t* idx, float* vmax,
@@ -59,8 +61,11 @@ cudaError_t launch_argmax_rows(const void* x, int64_t M, int V, int64_t ldx, int
 // (split-K, else 0), 256 x 256 tiles (0/1), whole tiles (0/1), K chunks per stage.
 void gemm_plan(int M, int N, int K, int num_sms, int* out);
 size_t gemm_workspace_bytes(int M, int N, int K, int num_sms);
+struct TpRows;
+// rp (optional): push each output row to its owner's receive slot (row-parallel
+// GEMM of tensor parallelism, see tp_rows.cuh) instead of writing y.
 cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,
                             void* y, int M, int N, int K, void* workspace, size_t workspace_bytes, int num_sms,
-                            cudaStream_t stream);
+                            cudaStream_t stream, const TpRows* rp = nullptr);
 
 }  // namespace ms

@@ -125,6 +125,23 @@ def fp8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Ten
     return y
 
 
+def fp8_gemm_rowpar(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor, bases, rank: int,
+                    world: int, max_rows: int) -> None:
+    """Row-parallel FP8 GEMM whose output rows go to their owners' receive slots in
+    the tensor-parallel buffers `bases` (ms_fp8_gemm_rowpar)."""
+    _cuda(xq, "xq")
+    M, K = xq.shape
+    N = wq.shape[0]
+    if wq.shape[1] != K or xq.dtype != FP8 or wq.dtype != FP8:
+        raise ValueError("fp8_gemm_rowpar: expected e4m3 xq [M, K] and wq [N, K]")
+    if not (xq.is_contiguous() and wq.is_contiguous()):
+        raise ValueError("fp8_gemm_rowpar: operands must be contiguous")
+    lib = _lib.load()
+    ws = workspace.get(lib.ms_fp8_gemm_workspace_size(M, N, K), xq.device, "gemm")
+    check(lib.ms_fp8_gemm_rowpar(ptr(xq), ptr(sx), ptr(wq), ptr(sw), M, N, K, ptr(ws), 0 if ws is None else ws.numel(),
+                                 bases, rank, world, max_rows, stream_ptr()), "ms_fp8_gemm_rowpar")
+
+
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
             want_fp16: bool = True, want_fp8: bool = False):
     """(residual +) RMSNorm with optional fp16 and FP8 outputs.

@@ -89,9 +89,10 @@ class Qwen3Attention(nn.Module):
         return self.o_proj(o.reshape(-1, self.num_heads * self.head_dim))
 
     def forward_fp8(self, positions: torch.Tensor, xq: torch.Tensor, sx: torch.Tensor,
-                    partial_out: torch.Tensor | None = None) -> torch.Tensor:
+                    tpf=None) -> torch.Tensor | None:
         """Fused FP8 path; xq/sx are the FP8 rows of the normed hidden states. With
-        partial_out the row-parallel o_proj writes its unreduced output there."""
+        tpf (tensor parallel, utils.tp_fused.TpFused) the row-parallel o_proj pushes
+        its output rows to their owners and nothing is returned."""
         ctx = get_context()
         attn = self.attn
         qkv = self.qkv_proj.forward_fp8(xq, sx)
@@ -103,7 +104,10 @@ class Qwen3Attention(nn.Module):
             (attn.k_cache, attn.v_cache, attn.k_scale_cache, attn.v_scale_cache), want_kv=want_kv)
         o = attn.forward_cached(q, k, v)
         oq, so = tp_quantize_rows(o.view(-1, self.q_size))
-        return self.o_proj.forward_fp8(oq, so, reduce=partial_out is None, out=partial_out)
+        if tpf is not None:
+            tpf.rowpar_gemm(oq, so, self.o_proj.weight_fp8, self.o_proj.weight_scale)
+            return None
+        return self.o_proj.forward_fp8(oq, so)
 
 
 class Qwen3MLP(nn.Module):
@@ -117,15 +121,17 @@ class Qwen3MLP(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return self.down_proj(self.act_fn(self.gate_up_proj(x)))
 
-    def forward_fp8(self, xq: torch.Tensor, sx: torch.Tensor, partial_out: torch.Tensor | None = None
-                    ) -> torch.Tensor:
+    def forward_fp8(self, xq: torch.Tensor, sx: torch.Tensor, tpf=None) -> torch.Tensor | None:
         gu = self.gate_up_proj.forward_fp8(xq, sx)
         if tp.exact_act_scale():
             a, _, _ = kernels.silu_mul(gu, want_fp16=True, want_fp8=False)
             aq, sa = tp_quantize_rows(a)
         else:
             aq, sa = self.act_fn.forward_fp8(gu)
-        return self.down_proj.forward_fp8(aq, sa, reduce=partial_out is None, out=partial_out)
+        if tpf is not None:
+            tpf.rowpar_gemm(aq, sa, self.down_proj.weight_fp8, self.down_proj.weight_scale)
+            return None
+        return self.down_proj.forward_fp8(aq, sa)
 
 
 class Qwen3DecoderLayer(nn.Module):
@@ -159,28 +165,29 @@ class Qwen3DecoderLayer(nn.Module):
         hidden_states = self.mlp(hidden_states)
         return hidden_states, residual
 
-    def forward_fp8(self, positions: torch.Tensor, hidden_states: torch.Tensor,
-                    residual: torch.Tensor | None, tpf=None) -> tuple[torch.Tensor, torch.Tensor]:
+    def forward_fp8(self, positions: torch.Tensor, hidden_states: torch.Tensor | None,
+                    residual: torch.Tensor | None, tpf=None) -> tuple[torch.Tensor | None, torch.Tensor]:
         """Fused FP8 layer. With tpf (utils.tp_fused.TpFused, tensor parallel) the
-        row-parallel outputs stay unreduced in the peer buffer and each sum + add +
-        RMSNorm + FP8 quantisation is one kernel; hidden_states is then the previous
-        layer's partial output and the residual is current on this rank's rows."""
-        rows = hidden_states.shape[0]
+        row-parallel GEMMs push their output rows to the ranks that own them and each
+        sum + add + RMSNorm + FP8 quantisation is one op; the layer then returns no
+        hidden state (the previous layer's output is in the peer buffers) and the
+        residual is current on this rank's rows."""
         if residual is None:
             xq, sx, _ = self.input_layernorm.forward_fp8(hidden_states)
             residual = hidden_states
         elif tpf is not None:
-            xq, sx = tpf.allreduce_norm_fp8(rows, residual, self.input_layernorm.weight, self.input_layernorm.eps)
+            rows = residual.shape[0]
+            xq, sx = tpf.allreduce_norm_fp8(rows, residual, self.input_layernorm.weight, self.input_layernorm.eps,
+                                            pushed=True)
         else:
             xq, sx, residual = self.input_layernorm.forward_fp8(hidden_states, residual)
-        part = tpf.partial(rows) if tpf is not None else None
-        h = self.self_attn.forward_fp8(positions, xq, sx, partial_out=part)
+        h = self.self_attn.forward_fp8(positions, xq, sx, tpf=tpf)
         if tpf is not None:
-            xq, sx = tpf.allreduce_norm_fp8(rows, residual, self.post_attention_layernorm.weight,
-                                            self.post_attention_layernorm.eps)
+            xq, sx = tpf.allreduce_norm_fp8(residual.shape[0], residual, self.post_attention_layernorm.weight,
+                                            self.post_attention_layernorm.eps, pushed=True)
         else:
             xq, sx, residual = self.post_attention_layernorm.forward_fp8(h, residual)
-        return self.mlp.forward_fp8(xq, sx, partial_out=part), residual
+        return self.mlp.forward_fp8(xq, sx, tpf=tpf), residual
 
 
 class Qwen3Model(nn.Module):
@@ -205,7 +212,7 @@ class Qwen3Model(nn.Module):
             else:
                 hidden_states, residual = layer(positions, hidden_states, residual)
         if tpf is not None:
-            return tpf.allreduce_norm_fp16(hidden_states.shape[0], residual, self.norm.weight, self.norm.eps)
+            return tpf.allreduce_norm_fp16(residual.shape[0], residual, self.norm.weight, self.norm.eps, pushed=True)
         return self.norm(hidden_states, residual)[0]
 
 

@@ -26,12 +26,12 @@ from microserve_b200._lib import check, stream_ptr
 from microserve_b200.utils import dist as tp
 
 FP8 = torch.float8_e4m3fn
-_PARTS = ("partial", "recv", "gq", "gs", "gh", "ctrl", "total")
+_PARTS = ("partial", "outq", "outs", "outh", "total")
 
 
 def layout(world: int, hidden: int, max_rows: int) -> dict[str, int]:
     """Byte offsets of one rank's buffer (the library's layout)."""
-    off = (C.c_int64 * 7)()
+    off = (C.c_int64 * 5)()
     check(_lib.load().ms_tp_layout(world, hidden, max_rows, off), "ms_tp_layout")
     return dict(zip(_PARTS, list(off)))
 
@@ -84,30 +84,43 @@ class TpFused:
             raise ValueError(f"TpFused holds {self.R} rows, {rows} requested")
         return self._view("partial", torch.float16, (self.R, self.H))[:rows]
 
-    def allreduce_norm_fp8(self, rows: int, residual: torch.Tensor, weight: torch.Tensor, eps: float
-                           ) -> tuple[torch.Tensor, torch.Tensor]:
-        """Sum the ranks' partial outputs, add the residual (rows owned by this rank
-        are updated in place), RMSNorm, FP8 row quantisation; every rank receives all
-        rows: returns (xq [rows, H] e4m3, sx [rows] fp32)."""
-        self._launch(rows, residual, weight, eps, want_h=False)
-        q = self._view("gq", FP8, (self.R, self.H))[:rows]
-        s = self._view("gs", torch.float32, (self.R,))[:rows]
+    def rowpar_gemm(self, xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor) -> None:
+        """The row-parallel FP8 GEMM (o_proj / down_proj shard) with each output row
+        pushed by the GEMM's epilogue to the rank that owns it (ms_fp8_gemm_rowpar);
+        the next allreduce_norm_* call takes pushed=True."""
+        from microserve_b200 import kernels
+        M, K = xq.shape
+        if wq.shape != (self.H, K):
+            raise ValueError(f"rowpar_gemm: weight must be [{self.H}, {K}]")
+        if M > self.R:
+            raise ValueError(f"TpFused holds {self.R} rows, {M} requested")
+        kernels.fp8_gemm_rowpar(xq, sx, wq, sw, self.bases, self.rank, self.world, self.R)
+
+    def allreduce_norm_fp8(self, rows: int, residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                           pushed: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+        """Sum the ranks' partial outputs (in `partial`, or already pushed by
+        rowpar_gemm), add the residual (rows owned by this rank are updated in place),
+        RMSNorm, FP8 row quantisation; every rank receives all rows: returns
+        (xq [rows, H] e4m3, sx [rows] fp32)."""
+        self._launch(rows, residual, weight, eps, want_h=False, pushed=pushed)
+        q = self._view("outq", FP8, (self.R, self.H))[:rows]
+        s = self._view("outs", torch.float32, (self.R,))[:rows]
         return q, s
 
-    def allreduce_norm_fp16(self, rows: int, residual: torch.Tensor, weight: torch.Tensor, eps: float
-                            ) -> torch.Tensor:
+    def allreduce_norm_fp16(self, rows: int, residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                            pushed: bool = False) -> torch.Tensor:
         """As allreduce_norm_fp8, returning the normalised fp16 rows [rows, H] (the final norm)."""
-        self._launch(rows, residual, weight, eps, want_h=True)
-        return self._view("gh", torch.float16, (self.R, self.H))[:rows]
+        self._launch(rows, residual, weight, eps, want_h=True, pushed=pushed)
+        return self._view("outh", torch.float16, (self.R, self.H))[:rows]
 
-    def _launch(self, rows, residual, weight, eps, want_h):
+    def _launch(self, rows, residual, weight, eps, want_h, pushed):
         if rows > self.R:
             raise ValueError(f"TpFused holds {self.R} rows, {rows} requested")
         if residual.shape != (rows, self.H) or residual.dtype != torch.float16 or not residual.is_contiguous():
             raise ValueError("residual must be a contiguous fp16 [rows, H] tensor")
         check(_lib.load().ms_tp_allreduce_rmsnorm_fp8(self.bases, self.rank, self.world, self.H, self.R,
                                                       residual.data_ptr(), weight.data_ptr(), rows, float(eps),
-                                                      1 if want_h else 0, stream_ptr()),
+                                                      1 if want_h else 0, 1 if pushed else 0, stream_ptr()),
               "ms_tp_allreduce_rmsnorm_fp8")
 
     def close(self) -> None:
