@@ -91,6 +91,7 @@ class ModelRunner:
         self.head_dim = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads
         self.num_layers = hf.num_hidden_layers
         self.max_model_len = min(config.max_model_len, hf.max_position_embeddings)
+        self.max_decode_blocks = (self.max_model_len + config.block_size - 1) // config.block_size
         self.vocab_size = hf.vocab_size
         if config.seed is not None:
             torch.manual_seed(config.seed)
@@ -192,12 +193,15 @@ class ModelRunner:
     def prepare_decode(self, seqs: list[Sequence]):
         """Host arrays of a decode batch: ids, positions, slots (int64), seqlens, tables (int32).
         slot = block_table[p // block_size] * block_size + p % block_size (model_runner.py:135-136
-        of the reference), read from the padded table of the batch."""
+        of the reference), read from the padded table of the batch. The tables always have
+        the width of max_model_len (as the captured graphs' tables do): the decode
+        attention's context split depends on that width, so eager and graph decodes of
+        the same batch then run the same split and give the same bits."""
         n = len(seqs)
         assert all(s.gap == 1 and s.num_scheduled_tokens == 1 for s in seqs)
         pos = np.fromiter((s.num_computed_tokens for s in seqs), dtype=np.int64, count=n)
         ids = np.fromiter((s.token_ids[s.num_computed_tokens] for s in seqs), dtype=np.int64, count=n)
-        bt = self._tables(seqs)
+        bt = self._tables(seqs, width=max(self.max_decode_blocks, max(len(s.block_table) for s in seqs)))
         bs = self.block_size
         blk = bt[np.arange(n), pos // bs]
         if (blk < 0).any():

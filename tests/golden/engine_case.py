@@ -48,6 +48,12 @@ def write_checkpoint(case: str, path: str) -> str:
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     tensors = {name: dummy_tensor(name, shape, SEED, dev).cpu().contiguous()
                for name, shape in checkpoint_shapes(cfg).items()}
+    # The tied head is written out as its own tensor: the reference converts its
+    # model with .to(dtype) after tying (microserve/engine/model_runner.py:56-57),
+    # which gives lm_head its own storage, so a checkpoint without lm_head.weight
+    # leaves the reference's head uninitialised. Both engines load it from here.
+    if cfg.tie_word_embeddings:
+        tensors["lm_head.weight"] = tensors["model.embed_tokens.weight"].clone()
     save_file(tensors, os.path.join(path, "model.safetensors"))
     del tensors
     torch.cuda.empty_cache() if torch.cuda.is_available() else None

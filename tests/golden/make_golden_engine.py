@@ -10,8 +10,12 @@ with pip --no-index --no-deps --target baseline/_ref); run once on a GPU box:
 
 Recorded per case and decode mode: every sequence's greedy tokens; for the small
 case also the logits row each token was taken from (fp16, the reference's own
-`_sample` input, microserve/engine/model_runner.py:15-34). Nothing in the test
-suite, smoke() or bench.py runs the reference; they read the committed file.
+`_sample` input, microserve/engine/model_runner.py:15-34), for the 0.6B case the
+two largest logits of each row. For the small case the CPU oracle is also run on
+the same checkpoint along the reference's token path, and its per-step distance
+to the reference is stored: the measured spread between two implementations of
+the same FP8 arithmetic. Nothing in the test suite, smoke() or bench.py runs the
+reference; they read the committed file.
 """
 from __future__ import annotations
 
@@ -35,7 +39,8 @@ def run_reference(case: str, path: str, eager: bool) -> dict:
 
     def spy(logits, seq):
         token = original(logits, seq)
-        seen.setdefault(seq.seq_id, []).append(logits.detach().half().cpu() if c["logits"] else None)
+        row = logits.detach()
+        seen.setdefault(seq.seq_id, []).append(row.half().cpu() if c["logits"] else row.float().topk(2).values.cpu())
         return token
 
     mr._sample = spy
@@ -49,6 +54,8 @@ def run_reference(case: str, path: str, eager: bool) -> dict:
         out = {"tokens": [s.completion_token_ids for s in seqs], "seconds": time.perf_counter() - t0}
         if c["logits"]:
             out["logits"] = torch.stack([torch.stack(seen[s.seq_id]) for s in seqs])  # [seqs, steps, V]
+        else:  # the two largest logits of every step: how close each greedy choice was to a tie
+            out["top2"] = torch.stack([torch.stack(seen[s.seq_id]) for s in seqs])  # [seqs, steps, 2]
         del eng
     finally:
         mr._sample = original

@@ -186,6 +186,7 @@ def _runner():
     from microserve_b200.engine.model_runner import ModelRunner
     r = object.__new__(ModelRunner)
     r.block_size = 256
+    r.max_decode_blocks = 8  # max_model_len 2048
     return r
 
 
@@ -197,7 +198,10 @@ def test_prepare_decode_matches_reference_formulas():
     assert ids.tolist() == [299, 1512, 5] and pos.tolist() == [299, 512, 0]
     ref = [O.slot_mapping(s.block_table, [p], 256)[0] for s, p in zip(seqs, [299, 512, 0])]
     assert slots.tolist() == ref and lens.tolist() == [300, 513, 1]
-    assert bt.dtype == np.int32 and np.array_equal(bt, O.block_table_rows([s.block_table for s in seqs]).numpy())
+    # decode tables are max_model_len wide (the graphs' width), padded with -1 like the reference's rows
+    rows = O.block_table_rows([s.block_table for s in seqs]).numpy()
+    assert bt.dtype == np.int32 and bt.shape == (3, 8)
+    assert np.array_equal(bt[:, :rows.shape[1]], rows) and (bt[:, rows.shape[1]:] == -1).all()
 
 
 def test_prepare_prefill_and_chunk_match_reference_formulas():
