@@ -554,7 +554,7 @@ def run_ours(args):
     step_bytes = w_layers + kv_bytes + head_bytes
 
     line = {
-        "metric": "output tok/s Qwen3-8B FP8 decode (FP8 KV), batch 256",
+        "metric": metric_name(args),
         "value": round(value, 1), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 acc, f16 activations",
@@ -704,6 +704,11 @@ def workload_config(args, ctx0) -> dict:
             "l2": "inputs larger than L2 (weights + KV >> 126 MB); no flush"}
 
 
+def metric_name(args) -> str:
+    """The metric both arms print (BASELINE's headline for the default config 3)."""
+    return f"output tok/s Qwen3-{args.model.upper()} FP8 decode (FP8 KV), batch {args.batch}"
+
+
 def reference_contexts(args) -> list[int]:
     """Context of each sequence at the first decode step: its prompt plus the token
     the prefill sampled (the GPU arm's batch["ctx0"])."""
@@ -775,7 +780,7 @@ def run_reference(args):
     sample = (f"whole decode steps of the full batch ({B} sequences, {L} decoder layers, LM head over "
               f"{V} tokens, greedy argmax) timed end to end; oracle/fp8_decoder.py (torch CPU) on "
               f"{threads} threads")
-    line = {"impl": "reference", "metric": "output tok/s Qwen3-8B FP8 decode (FP8 KV), batch 256",
+    line = {"impl": "reference", "metric": metric_name(args),
             "value": round(value, 3), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 2), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (CPU fp32 math)",

@@ -11,10 +11,10 @@ with pip --no-index --no-deps --target baseline/_ref); run once on a GPU box:
 Recorded per case and decode mode: every sequence's greedy tokens; for the small
 case also the logits row each token was taken from (fp16, the reference's own
 `_sample` input, microserve/engine/model_runner.py:15-34), for the 0.6B case the
-two largest logits of each row. For the small case the CPU oracle is also run on
-the same checkpoint along the reference's token path, and its per-step distance
-to the reference is stored: the measured spread between two implementations of
-the same FP8 arithmetic. Nothing in the test suite, smoke() or bench.py runs the
+two largest logits of each row. The CPU oracle is also run on each checkpoint
+along the reference's token path, and its per-step distance to the reference is
+stored: the measured spread between two implementations of the same FP8
+arithmetic. Nothing in the test suite, smoke() or bench.py runs the
 reference; they read the committed file.
 """
 from __future__ import annotations
@@ -39,8 +39,7 @@ def run_reference(case: str, path: str, eager: bool) -> dict:
 
     def spy(logits, seq):
         token = original(logits, seq)
-        row = logits.detach()
-        seen.setdefault(seq.seq_id, []).append(row.half().cpu() if c["logits"] else row.float().topk(2).values.cpu())
+        seen.setdefault(seq.seq_id, []).append(logits.detach().half().cpu())
         return token
 
     mr._sample = spy
@@ -52,10 +51,10 @@ def run_reference(case: str, path: str, eager: bool) -> dict:
             eng.step()
         torch.cuda.synchronize()
         out = {"tokens": [s.completion_token_ids for s in seqs], "seconds": time.perf_counter() - t0}
-        if c["logits"]:
-            out["logits"] = torch.stack([torch.stack(seen[s.seq_id]) for s in seqs])  # [seqs, steps, V]
-        else:  # the two largest logits of every step: how close each greedy choice was to a tie
-            out["top2"] = torch.stack([torch.stack(seen[s.seq_id]) for s in seqs])  # [seqs, steps, 2]
+        # [seqs, steps, V]; kept in the file for the small case only (the 0.6B case keeps
+        # the two largest logits of every step: how close each greedy choice was to a tie)
+        out["logits"] = torch.stack([torch.stack(seen[s.seq_id]) for s in seqs])
+        out["top2"] = out["logits"].float().topk(2, dim=-1).values
         del eng
     finally:
         mr._sample = original
@@ -126,17 +125,20 @@ def main(out_path: str, scratch: str) -> None:
         result[case] = runs
         result["meta"][f"{case}_eager_vs_graph_token_agreement"] = agree
         print(case, "eager vs graph token agreement", agree, flush=True)
-        if CASES[case]["logits"]:
-            # how far the oracle (CPU restatement) is from the reference engine on the same path
-            ref = runs["eager"]["logits"].float()
-            orc = torch.stack(oracle_logits(case, path, runs["eager"]["tokens"])).float()
-            rel = ((orc - ref).norm(dim=-1) / ref.norm(dim=-1))  # [seqs, steps]
-            top2 = ref.topk(2, dim=-1).values
-            result["meta"][f"{case}_oracle_vs_reference"] = {
-                "rel_l2_per_step": rel, "argmax_agree": (orc.argmax(-1) == ref.argmax(-1)).float().mean().item(),
-                "reference_top1_margin": top2[..., 0] - top2[..., 1]}
-            print(case, "oracle vs reference: max rel-L2", rel.max().item(), "median", rel.median().item(),
-                  "argmax agreement", result["meta"][f"{case}_oracle_vs_reference"]["argmax_agree"], flush=True)
+        # how far the oracle (CPU restatement) is from the reference engine on the same path
+        ref = runs["eager"]["logits"].float()
+        orc = torch.stack(oracle_logits(case, path, runs["eager"]["tokens"])).float()
+        rel = ((orc - ref).norm(dim=-1) / ref.norm(dim=-1))  # [seqs, steps]
+        top2 = ref.topk(2, dim=-1).values
+        result["meta"][f"{case}_oracle_vs_reference"] = {
+            "rel_l2_per_step": rel, "max_abs_diff_per_step": (orc - ref).abs().amax(-1),
+            "argmax_agree": (orc.argmax(-1) == ref.argmax(-1)).float().mean().item(),
+            "reference_top1_margin": top2[..., 0] - top2[..., 1]}
+        print(case, "oracle vs reference: max rel-L2", rel.max().item(), "median", rel.median().item(),
+              "argmax agreement", result["meta"][f"{case}_oracle_vs_reference"]["argmax_agree"], flush=True)
+        if not CASES[case]["logits"]:
+            for mode in runs:
+                del runs[mode]["logits"]
         shutil.rmtree(path, ignore_errors=True)
     torch.save(result, out_path)
     print("wrote", out_path)

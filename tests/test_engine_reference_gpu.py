@@ -24,7 +24,8 @@ to the reference as tightly as the reference's own arithmetic, restated, holds:
   * per-step logits relative L2: median and maximum within 1.25x of the oracle's;
   * greedy choices: at least 90 % identical, and wherever they differ the reference's
     top-1 margin is smaller than the largest logit difference in that row (a near-tie);
-  * free-running tokens identical up to the first such near-tie;
+  * free-running tokens identical up to the first such near-tie (on the 0.6B model: a
+    step where the reference's margin is smaller than the oracle's logit difference);
   * eager and CUDA-graph decodes of this engine produce identical tokens."""
 import pytest
 import torch
@@ -146,12 +147,19 @@ def test_qwen3_0_6b_tokens_follow_reference_until_a_near_tie(tmp_path):
         torch.cuda.empty_cache()
     assert tokens["eager"] == tokens["graph"], "eager and CUDA-graph decodes differ"
     ref = _ref()["0.6b"]["graph"]
-    agree = []
+    orc = _ref()["meta"]["0.6b_oracle_vs_reference"]
+    agree, margins = [], []
     for s, (ours, theirs) in enumerate(zip(tokens["graph"], ref["tokens"])):
         k = _first_divergence(ours, theirs)
         agree.append(32 if k is None else k)
         if k is not None:
+            # a near-tie: up to step k this run followed the reference's token path, as the
+            # oracle did; the reference's top-1 margin at k is smaller than the logit
+            # difference the oracle shows there (or typically shows on this model)
             top2 = ref["top2"][s, k]
-            # the largest per-row logit difference measured on the small case is about 0.16
-            assert top2[0] - top2[1] < 0.16, f"seq {s}: tokens diverge at step {k} away from a near-tie"
-    print("0.6b: identical greedy tokens before the first near-tie:", agree)
+            margin = (top2[0] - top2[1]).item()
+            spread = max(orc["max_abs_diff_per_step"][s, k].item(), orc["max_abs_diff_per_step"].median().item())
+            margins.append((round(margin, 4), round(spread, 4)))
+            assert margin < spread, f"seq {s}: tokens diverge at step {k} away from a near-tie"
+    print("0.6b: identical greedy tokens before the first near-tie:", agree,
+          "(reference margin, oracle logit spread) there:", margins)
