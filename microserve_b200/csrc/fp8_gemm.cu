@@ -967,7 +967,10 @@ struct Plan {
 //    projection) for M <= 256: split-K. One token tile of BN = M rounded
 //    up to 32/64/96/128/192/256, `splits` = SMs / weight tiles (<= 8) CTAs per
 //    tile, each streaming 1/splits of K once; the partials are reduced in a
-//    balanced way (each CTA finishes a slice of the tile).
+//    balanced way (each CTA finishes a slice of the tile). With 129..256 tokens
+//    and 8..23 K steps (few weight tiles: the q/k/v shards of tensor parallelism)
+//    4 K parts over 64-token tiles instead (128-token tiles when 64-token ones
+//    would fill more than 2/3 of the SMs).
 //  * 129..256 tokens with more 128-row weight tiles than SMs (the gate/up
 //    projection): 256 x 256 tiles of fp8_gemm_wide_kernel, dealt whole.
 //  * Other decode shapes: BN = M up to 128; for 129..256 tokens the smallest of
@@ -999,6 +1002,17 @@ Plan make_plan(int M, int N, int K, int num_sms) {
     // three quarters of the SMs idle (the small shards of tensor parallelism).
     const int64_t dp_tiles = tiles_n * ((M + kBM - 1) / kBM);
     if (s >= 2 && steps >= 2 && (M <= 128 || steps >= 24 || 4 * dp_tiles < num_sms)) {
+      if (M > 128 && steps < 24 && steps >= 8) {
+        // few weight tiles (the q/k/v shard of tensor parallelism): 4 K parts over
+        // narrower token tiles (256 x 768 x 4096: 64-token tiles 8.0 us vs one
+        // 256-token tile in 8 parts 10.8 us; 256 x 1536 x 4096: 128-token tiles 9.7
+        // vs 11.9 us, B200 sweep); 64-token tiles while they fill at most 2/3 of the SMs
+        const int64_t t64 = tiles_n * ((M + 63) / 64);
+        p.bn = 3 * 4 * t64 <= 2 * (int64_t)num_sms ? 64 : 128;
+        p.splits = 4;
+        p.ctas = (int)(tiles_n * ((M + p.bn - 1) / p.bn) * p.splits);
+        return p;
+      }
       p.bn = full;
       // every K part must hold at least one step: an empty part would hand over an
       // accumulator the MMA never wrote

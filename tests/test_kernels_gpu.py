@@ -86,8 +86,9 @@ GEMM_SHAPES = [
     # 256-row x 256-token tiles (129..256 tokens, more 128-row weight tiles than SMs), ragged last tile;
     # the 8B gate/up projection first; (160, 40000, 640) deals two tiles to some CTAs
     (256, 24576, 4096), (256, 24576, 1024), (200, 19000, 512), (160, 40000, 640), (129, 24576, 272),
-    # tensor-parallel shards: few weight tiles at 256 tokens (split-K)
-    (256, 768, 4096), (256, 4096, 512),
+    # tensor-parallel shards: few weight tiles at 256 tokens (split-K over 64- and 128-token tiles, a ragged
+    # last token tile, and one 256-token tile in 8 parts)
+    (256, 768, 4096), (256, 1536, 4096), (200, 768, 4096), (129, 1536, 2048), (256, 768, 2048), (256, 4096, 512),
     # 129..256 tokens dealt as 64- / 96-token tiles (o and qkv projections at 256 tokens, a ragged last tile)
     (256, 4096, 4096), (160, 4096, 2048),
     # N % 8 != 0: rows of y not 16-byte aligned, so the last tile is stored directly (no bulk store)

@@ -59,6 +59,9 @@ def test_gemm_schedules_of_the_8b_decode_and_prefill_shapes():
     assert _plan(256, 24576, 4096) == dict(bn=256, ctas=96, splits=0, wide=1, dp=1, ch=1)
     # down (long K): split-K, 32 weight tiles x 4 K parts
     assert _plan(256, 4096, 12288) == dict(bn=256, ctas=128, splits=4, wide=0, dp=0, ch=2)
+    # tensor-parallel q/k/v shards at 256 tokens: 4 K parts over 64- / 128-token tiles
+    assert _plan(256, 768, 4096) == dict(bn=64, ctas=96, splits=4, wide=0, dp=0, ch=2)
+    assert _plan(256, 1536, 4096) == dict(bn=128, ctas=96, splits=4, wide=0, dp=0, ch=2)
     # one token: split-K with a 32-token tile, 3 K parts per weight tile
     assert _plan(1, 6144, 4096) == dict(bn=32, ctas=144, splits=3, wide=0, dp=0, ch=2)
     # prefill: 256-token tiles, whole tiles when they fill the SMs evenly
