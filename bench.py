@@ -377,23 +377,20 @@ def kernel_rooflines(engine, batch, step_idx, hbm_peak):
             res["tp_allreduce_rmsnorm_fp8"] = dict(seconds=t, bytes=(world - 1) * R * (2 * H + H + 4), per_layer=2,
                                                    bound="nvlink", peak_gbs=NVLINK_PEER_GBS)
         if tpf is not None:
-            # o_proj as the decode step runs it: the row-parallel GEMM pushing its output rows
-            # to their owners (overlapping the transfer with the GEMM) + the op that reduces,
-            # normalises and gathers. Communication hidden = 1 - exposed / standalone, with
-            # exposed = pair - (local GEMM + the norm alone) and standalone = op - norm alone.
+            # o_proj as the decode step runs it: ONE kernel, the row-parallel GEMM pushing its
+            # output rows to their owners (the transfer overlaps the GEMM), then reducing,
+            # normalising and gathering. Communication hidden = 1 - exposed / standalone, with
+            # exposed = fused - (local GEMM + the norm alone) and standalone = op - norm alone.
             o = layer.self_attn.o_proj
             xo = torch.randn(B, o.in_features, device=dev, generator=g).half()
             oq, so = kernels.quantize_rows_fp8(xo)
             sync_all()
 
-            def pair():
-                tpf.rowpar_gemm(oq, so, o.weight_fp8, o.weight_scale)
-                tpf.allreduce_norm_fp8(B, res_rows, w, eps, pushed=True)
-            t = time_kernel(pair)
+            t = time_kernel(lambda: tpf.rowpar_gemm_norm(oq, so, o.weight_fp8, o.weight_scale, res_rows, w, eps))
             op_t = res["tp_allreduce_rmsnorm_fp8"]["seconds"]
             norm_t, gemm_t = res["rmsnorm_fp8"]["seconds"], res["o_proj"]["seconds"]
             exposed = max(0.0, t - gemm_t - norm_t)
-            res["tp_o_proj_pushed_pair"] = dict(
+            res["tp_o_proj_gemm_allreduce_rmsnorm_fp8"] = dict(
                 seconds=t, bytes=(world - 1) * R * (2 * H + H + 4), per_layer=1, bound="nvlink",
                 peak_gbs=NVLINK_PEER_GBS,
                 comm_hidden_frac=round(1.0 - min(1.0, exposed / max(op_t - norm_t, 1e-9)), 3))
@@ -812,8 +809,10 @@ def run_tp_rowpar_sweep(args):
     """BASELINE config 5, the fused row-parallel op under torchrun: for each M, the
     row-parallel FP8 GEMM with N = hidden, K = intermediate / TP (down_proj of the
     --model's shapes; 32B: N = 5120, K = 25600 / TP) pushing its output rows to their
-    owners + the all-reduce / residual / RMSNorm / FP8 op, against this rank's GEMM
-    writing locally + NCCL all-reduce + the RMSNorm/FP8 kernel. bf16/fp16 activations
+    owners and then reducing / adding / normalising / quantising them
+    (ms_fp8_gemm_rowpar_ar_rmsnorm: one kernel for decode-sized M, the GEMM + the op
+    for larger M), against this rank's GEMM writing locally + NCCL all-reduce + the
+    RMSNorm/FP8 kernel. bf16/fp16 activations
     N(0, 1). Device time per call (CUDA graph of 20 calls, max over ranks); NVLink
     bytes each rank sends per call: its partial rows to their owners and its codes to
     every peer."""
@@ -845,8 +844,7 @@ def run_tp_rowpar_sweep(args):
         y = torch.empty(M, H, device=dev, dtype=torch.float16)
 
         def fused():
-            f.rowpar_gemm(xq, sx, wq, sw)
-            f.allreduce_norm_fp8(M, res, nw, 1e-6, pushed=True)
+            f.rowpar_gemm_norm(xq, sx, wq, sw, res, nw, 1e-6)
 
         def baseline():
             kernels.fp8_gemm(xq, sx, wq, sw, out=y)

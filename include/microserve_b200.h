@@ -253,6 +253,23 @@ int ms_fp8_gemm_rowpar(const void* xq, const float* sx, const void* wq, const fl
                        int64_t K, void* workspace, size_t workspace_bytes, void* const* bases, int rank, int world,
                        int64_t max_rows, void* stream);
 
+/* ms_fp8_gemm_rowpar + ms_tp_allreduce_rmsnorm_fp8(..., pushed = 1) as ONE kernel
+ * per rank: the row-parallel FP8 GEMM pushes its output rows to their owners from
+ * its epilogue, then each CTA, once its tiles are out, reduces its share of this
+ * rank's rows (rank order, fp32), adds the residual, normalises (weight, eps),
+ * quantises and sends the rows to every rank (codes + scales, or fp16 rows with
+ * want_fp16) - outputs and semantics exactly those of the two calls, in the out
+ * areas of ms_tp_layout. When the row work does not fit the GEMM's tail (hidden
+ * > 6144, or more than two owned rows per GEMM CTA - prefill-sized M) the call
+ * launches the two kernels instead. Replaces RowParallelLinear + its
+ * dist.all_reduce (microserve/layers/linear.py:70-77; FP8DynamicLinear.forward,
+ * layers/fp8_linear.py:64-80) + the add/RMSNorm after it (layers/layernorm.py:22-42)
+ * + the next activation quantisation (layers/fp8_linear.py:14-23). */
+int ms_fp8_gemm_rowpar_ar_rmsnorm(const void* xq, const float* sx, const void* wq, const float* sw, int64_t M,
+                                  int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* const* bases,
+                                  int rank, int world, int64_t max_rows, void* residual, const void* weight,
+                                  float eps, int want_fp16, void* stream);
+
 /* Upper bound, in nanoseconds, of every in-kernel wait on the current device
  * (peer data, pipeline barriers); default 4e9. A wait that runs out records a
  * device status and the kernel returns. Set it outside stream capture; it

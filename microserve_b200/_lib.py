@@ -33,6 +33,8 @@ SIGNATURES: dict[str, tuple] = {
     "ms_tp_allreduce_rmsnorm_fp8": (i32, [vp, i32, i32, i64, i64, vp, vp, i64, f32, i32, i32, vp]),
     "ms_set_wait_limit": (i32, [C.c_uint64]),
     "ms_fp8_gemm_rowpar": (i32, [vp, vp, vp, vp, i64, i64, i64, vp, sz, vp, i32, i32, i64, vp]),
+    "ms_fp8_gemm_rowpar_ar_rmsnorm": (i32, [vp, vp, vp, vp, i64, i64, i64, vp, sz, vp, i32, i32, i64, vp, vp, f32,
+                                           i32, vp]),
     "ms_row_amax": (i32, [vp, i64, i64, i64, vp, vp]),
     "ms_quantize_rows_fp8_amax": (i32, [vp, i64, i64, i64, vp, vp, vp, vp]),
     "ms_argmax_rows": (i32, [vp, i64, i64, i64, vp, vp, vp, sz, vp]),

@@ -371,6 +371,47 @@ int ms_fp8_gemm_rowpar(const void* xq, const float* sx, const void* wq, const fl
                     "ms_fp8_gemm_rowpar");
 }
 
+int ms_fp8_gemm_rowpar_ar_rmsnorm(const void* xq, const float* sx, const void* wq, const float* sw, int64_t M,
+                                  int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* const* bases,
+                                  int rank, int world, int64_t max_rows, void* residual, const void* weight,
+                                  float eps, int want_fp16, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0 || M > max_rows || max_rows > INT32_MAX || N > 16384 || K > INT32_MAX ||
+      world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(MS_ERR_INVALID, "ms_fp8_gemm_rowpar_ar_rmsnorm: bad sizes M=%lld N=%lld K=%lld rank=%d world=%d",
+                (long long)M, (long long)N, (long long)K, rank, world);
+  if (M == 0) return MS_OK;
+  if (N % 16 != 0 || K % 16 != 0)
+    return fail(MS_ERR_UNSUPPORTED, "ms_fp8_gemm_rowpar_ar_rmsnorm: N and K must be multiples of 16");
+  if (!xq || !sx || !wq || !sw || !bases || !residual || !weight)
+    return fail(MS_ERR_INVALID, "ms_fp8_gemm_rowpar_ar_rmsnorm: null pointer");
+  for (int p = 0; p < world; ++p)
+    if (!bases[p] || ((uintptr_t)bases[p] & 255) != 0)
+      return fail(MS_ERR_INVALID, "ms_fp8_gemm_rowpar_ar_rmsnorm: buffer of rank %d null or not 256-byte aligned",
+                  p);
+  if (((uintptr_t)residual & 15) != 0 || ((uintptr_t)weight & 15) != 0)
+    return fail(MS_ERR_INVALID, "ms_fp8_gemm_rowpar_ar_rmsnorm: residual/weight not 16-byte aligned");
+  const size_t need = ms::gemm_workspace_bytes((int)M, (int)N, (int)K, num_sms());
+  if (workspace_bytes < need || (need > 0 && workspace == nullptr))
+    return fail(MS_ERR_WORKSPACE, "ms_fp8_gemm_rowpar_ar_rmsnorm: workspace %zu < %zu bytes", workspace_bytes,
+                need);
+  ms::TpRows rp = ms::tp_rows_args(bases, rank, world, N, max_rows, (int)M);
+  rp.residual = static_cast<__half*>(residual);
+  rp.weight = static_cast<const __half*>(weight);
+  rp.eps = eps;
+  rp.want_h = want_fp16 ? 1 : 0;
+  rp.pushed = 1;
+  bool tail = true;
+  const int rc = check_cuda(ms::launch_fp8_gemm(xq, sx, wq, sw, nullptr, nullptr, (int)M, (int)N, (int)K, workspace,
+                                                workspace_bytes, num_sms(), S(stream), &rp, &tail),
+                            "ms_fp8_gemm_rowpar_ar_rmsnorm");
+  if (rc != MS_OK || tail) return rc;
+  // the row work did not fit the GEMM's tail (many rows per CTA, or a very wide row):
+  // the separate op on the pushed rows
+  return check_cuda(ms::launch_tp_allreduce_rmsnorm_fp8(bases, rank, world, N, max_rows, residual, weight, (int)M,
+                                                        eps, want_fp16, 1, num_sms(), S(stream)),
+                    "ms_fp8_gemm_rowpar_ar_rmsnorm");
+}
+
 int ms_set_wait_limit(uint64_t ns) {
   if (ns == 0) return fail(MS_ERR_INVALID, "ms_set_wait_limit: limit must be > 0");
   const unsigned long long v = ns;

@@ -65,6 +65,12 @@ struct GemmArgs {
   const int* rp_ctrl;
   int64_t rp_half, rp_src;  // elements of one parity set / of one source's slots
   int rp_R, rp_rank;
+  // rp_tail: after its tiles, every CTA also does the tensor-parallel row work
+  // (reduce + residual + RMSNorm + FP8, gather; tp_rows.cuh) for the row indices
+  // j = CTA, CTA + grid, ... < R, so the whole row-parallel linear + all-reduce +
+  // norm is this one kernel. Needs every CTA of the grid resident (grid <= SMs).
+  int rp_tail, rp_nvt;
+  TpRows tail;
 };
 
 // BN: token columns per tile (MMA N). CH: 128-byte K chunks per pipeline stage.
@@ -129,6 +135,28 @@ __device__ __forceinline__ void tma_store_2d_wait(const CUtensorMap* map, uint32
                : "memory");
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// The tensor-parallel row work at the end of a row-parallel GEMM (rp_tail): runs on
+// all threads of the CTA once its tiles are pushed; the stage buffers are free by
+// then and hold the staged row (smem >= H * 2 + 256 bytes).
+template <int NVT>
+__device__ __noinline__ void rowpar_tail(const TpRows& a, unsigned char* smem) {
+  H8* srow = reinterpret_cast<H8*>(smem);
+  float* red_ss = reinterpret_cast<float*>(smem + a.H * 2);
+  float* red_max = red_ss + kMaxRowWarps;
+  int* s_e = reinterpret_cast<int*>(red_max + 32);
+  // no CTA can advance the epoch before this one arrives, so this is the call's epoch
+  if (threadIdx.x == 0) *s_e = *reinterpret_cast<volatile int*>(a.ctrl);
+  __syncthreads();
+  const int e = *s_e, b = e & 1;
+  const uint64_t limit = wait_limit_ns();
+  bool fail = false;
+  for (int j = blockIdx.x; j < a.R && !fail; j += gridDim.x)
+    if (a.rank * a.R + j < a.M) fail = !tp_reduce_row<NVT>(a, j, b, limit, srow, red_ss, red_max);
+  for (int j = blockIdx.x; j < a.R && !fail; j += gridDim.x) fail = !tp_collect_rows(a, j, b, limit);
+  fail = __syncthreads_or(fail) != 0;
+  if (threadIdx.x == 0) tp_finish_call(a, fail, e);
 }
 
 // Row-parallel destination of output row m (rank m / R's receive slot for this rank).
@@ -396,7 +424,7 @@ __device__ __forceinline__ void split_epilogue(const GemmArgs& args, uint32_t ac
 template <int BN, int CH>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                    const __grid_constant__ CUtensorMap tmap_y, GemmArgs args) {
+                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ GemmArgs args) {
   using C = Cfg<BN, CH>;
   static_assert(C::kStages * C::kStageBytes >= BN * kBM * 2, "staged output tile fits the stages");
   // The 128B swizzle atoms need 1024-byte alignment. The dynamic window is only
@@ -647,6 +675,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
   }
+  if (args.rp_tail) {  // this CTA's tiles are all pushed: its share of the row work
+    __syncwarp();
+    switch (args.rp_nvt) {
+      case 1: rowpar_tail<1>(args.tail, smem); break;
+      case 2: rowpar_tail<2>(args.tail, smem); break;
+      case 3: rowpar_tail<3>(args.tail, smem); break;
+      default: rowpar_tail<4>(args.tail, smem); break;
+    }
+  }
 }
 
 // Wide tiles for decode batches of 129..256 tokens with many weight tiles (the
@@ -669,7 +706,7 @@ static_assert(2 * kWideBN * kBM * 2 <= kWideStages * kWideStageBytes, "staged ou
 
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                         const __grid_constant__ CUtensorMap tmap_y, GemmArgs args) {
+                         const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ GemmArgs args) {
   extern __shared__ __align__(16) unsigned char smem_raw[];  // aligned by hand, see fp8_gemm_kernel
   const uint32_t raw_addr = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
@@ -1083,7 +1120,7 @@ size_t gemm_workspace_bytes(int M, int N, int K, int num_sms) {
 
 cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,
                             void* y, int M, int N, int K, void* workspace, size_t workspace_bytes, int num_sms,
-                            cudaStream_t stream, const TpRows* rp) {
+                            cudaStream_t stream, const TpRows* rp, bool* tail) {
   if (M == 0 || N == 0) return cudaSuccess;
   if (rp != nullptr && (K % 16 != 0 || rp->H != N || rp->M != M)) return cudaErrorInvalidValue;
   if (K % 16 != 0) {
@@ -1132,6 +1169,20 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
     args.rp_src = rp->recv_src;
     args.rp_R = rp->R;
     args.rp_rank = rp->rank;
+    // the row work in the GEMM's own tail: every CTA resident (all plans here use at
+    // most one CTA per SM), at most two owned rows per CTA, the canonical RMSNorm
+    // layout (32 W threads) and a row (<= 4 vectors per thread) within 192 threads
+    const int nv = N / 8;
+    if (tail != nullptr && *tail) {
+      *tail = p.ctas <= num_sms && rp->R <= 2 * p.ctas && 32 * row_warps(nv) <= kThreads && nv <= 4 * kThreads;
+      if (*tail) {
+        args.rp_tail = 1;
+        args.rp_nvt = (nv + kThreads - 1) / kThreads;
+        args.tail = *rp;
+      }
+    }
+  } else if (tail != nullptr) {
+    *tail = false;
   }
   args.M = M;
   args.N = N;

@@ -63,9 +63,12 @@ void gemm_plan(int M, int N, int K, int num_sms, int* out);
 size_t gemm_workspace_bytes(int M, int N, int K, int num_sms);
 struct TpRows;
 // rp (optional): push each output row to its owner's receive slot (row-parallel
-// GEMM of tensor parallelism, see tp_rows.cuh) instead of writing y.
+// GEMM of tensor parallelism, see tp_rows.cuh) instead of writing y. tail (with
+// rp): in, a request to do the tensor-parallel row work (reduce + residual +
+// RMSNorm + FP8 + gather, the fields of *rp) in the GEMM's own tail; out, whether
+// it will (otherwise the caller launches the separate op with pushed rows).
 cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,
                             void* y, int M, int N, int K, void* workspace, size_t workspace_bytes, int num_sms,
-                            cudaStream_t stream, const TpRows* rp = nullptr);
+                            cudaStream_t stream, const TpRows* rp = nullptr, bool* tail = nullptr);
 
 }  // namespace ms

@@ -142,6 +142,26 @@ def fp8_gemm_rowpar(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: to
                                  bases, rank, world, max_rows, stream_ptr()), "ms_fp8_gemm_rowpar")
 
 
+def fp8_gemm_rowpar_ar_rmsnorm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor, bases,
+                               rank: int, world: int, max_rows: int, residual: torch.Tensor, weight: torch.Tensor,
+                               eps: float, want_fp16: bool) -> None:
+    """Row-parallel FP8 GEMM + all-reduce + residual + RMSNorm + FP8 (or fp16) rows in one
+    kernel over the tensor-parallel buffers `bases` (ms_fp8_gemm_rowpar_ar_rmsnorm)."""
+    _cuda(xq, "xq")
+    M, K = xq.shape
+    N = wq.shape[0]
+    if wq.shape[1] != K or xq.dtype != FP8 or wq.dtype != FP8:
+        raise ValueError("fp8_gemm_rowpar_ar_rmsnorm: expected e4m3 xq [M, K] and wq [N, K]")
+    if not (xq.is_contiguous() and wq.is_contiguous()):
+        raise ValueError("fp8_gemm_rowpar_ar_rmsnorm: operands must be contiguous")
+    lib = _lib.load()
+    ws = workspace.get(lib.ms_fp8_gemm_workspace_size(M, N, K), xq.device, "gemm")
+    check(lib.ms_fp8_gemm_rowpar_ar_rmsnorm(ptr(xq), ptr(sx), ptr(wq), ptr(sw), M, N, K, ptr(ws),
+                                            0 if ws is None else ws.numel(), bases, rank, world, max_rows,
+                                            ptr(residual), ptr(weight), float(eps), 1 if want_fp16 else 0,
+                                            stream_ptr()), "ms_fp8_gemm_rowpar_ar_rmsnorm")
+
+
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
             want_fp16: bool = True, want_fp8: bool = False):
     """(residual +) RMSNorm with optional fp16 and FP8 outputs.

@@ -12,11 +12,15 @@ reference's, so checkpoints load the same way. Two forwards exist:
     2. FP8 GEMM  qkv                                  (qkv_proj)
     3. q/k RMSNorm + RoPE + FP8 KV store              (qwen3.py:49-53, attention.py:41-43)
     4. attention (decode / prefill / chunk)           (attention.py:44-60)
-    5. FP8 row quant of o + FP8 GEMM o_proj (+ TP sum)
+    5. FP8 row quant of o + FP8 GEMM o_proj
     6. residual + RMSNorm -> FP8 rows                 (post_attention_layernorm + act quant)
     7. FP8 GEMM gate_up
     8. SiLU*mul -> FP8 rows                           (act_fn + down_proj act quant)
-    9. FP8 GEMM down_proj (+ TP sum)
+    9. FP8 GEMM down_proj
+  With tensor parallelism over peer memory, 5+6 and 9+(the next layer's 1, or
+  the final norm) are each ONE kernel: the row-parallel GEMM pushes its output
+  rows to the ranks that own them and then sums, adds, normalises and gathers
+  (Qwen3DecoderLayer.forward_tp).
   Every intermediate rounding matches the reference's module path: each
   fused FP8 producer quantises exactly the fp16 tensor the reference would
   have materialised and then quantised.
@@ -88,11 +92,12 @@ class Qwen3Attention(nn.Module):
         o = self.attn(q, k, v)
         return self.o_proj(o.reshape(-1, self.num_heads * self.head_dim))
 
-    def forward_fp8(self, positions: torch.Tensor, xq: torch.Tensor, sx: torch.Tensor,
-                    tpf=None) -> torch.Tensor | None:
+    def forward_fp8(self, positions: torch.Tensor, xq: torch.Tensor, sx: torch.Tensor, tpf=None, norm=None,
+                    residual: torch.Tensor | None = None):
         """Fused FP8 path; xq/sx are the FP8 rows of the normed hidden states. With
-        tpf (tensor parallel, utils.tp_fused.TpFused) the row-parallel o_proj pushes
-        its output rows to their owners and nothing is returned."""
+        tpf (tensor parallel, utils.tp_fused.TpFused) o_proj is one kernel with the
+        all-reduce, the residual add and `norm` (the post-attention RMSNorm): it
+        returns the FP8 rows (xq, sx) of the next input instead of o_proj's output."""
         ctx = get_context()
         attn = self.attn
         qkv = self.qkv_proj.forward_fp8(xq, sx)
@@ -105,8 +110,8 @@ class Qwen3Attention(nn.Module):
         o = attn.forward_cached(q, k, v)
         oq, so = tp_quantize_rows(o.view(-1, self.q_size))
         if tpf is not None:
-            tpf.rowpar_gemm(oq, so, self.o_proj.weight_fp8, self.o_proj.weight_scale)
-            return None
+            return tpf.rowpar_gemm_norm(oq, so, self.o_proj.weight_fp8, self.o_proj.weight_scale, residual,
+                                        norm.weight, norm.eps)
         return self.o_proj.forward_fp8(oq, so)
 
 
@@ -121,7 +126,11 @@ class Qwen3MLP(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return self.down_proj(self.act_fn(self.gate_up_proj(x)))
 
-    def forward_fp8(self, xq: torch.Tensor, sx: torch.Tensor, tpf=None) -> torch.Tensor | None:
+    def forward_fp8(self, xq: torch.Tensor, sx: torch.Tensor, tpf=None, norm=None,
+                    residual: torch.Tensor | None = None, want_fp16: bool = False):
+        """With tpf (tensor parallel) down_proj is one kernel with the all-reduce, the
+        residual add and `norm` (the next layer's input RMSNorm or the final norm): it
+        returns the next FP8 rows (xq, sx), or with want_fp16 the normalised fp16 rows."""
         gu = self.gate_up_proj.forward_fp8(xq, sx)
         if tp.exact_act_scale():
             a, _, _ = kernels.silu_mul(gu, want_fp16=True, want_fp8=False)
@@ -129,8 +138,8 @@ class Qwen3MLP(nn.Module):
         else:
             aq, sa = self.act_fn.forward_fp8(gu)
         if tpf is not None:
-            tpf.rowpar_gemm(aq, sa, self.down_proj.weight_fp8, self.down_proj.weight_scale)
-            return None
+            return tpf.rowpar_gemm_norm(aq, sa, self.down_proj.weight_fp8, self.down_proj.weight_scale, residual,
+                                        norm.weight, norm.eps, want_fp16=want_fp16)
         return self.down_proj.forward_fp8(aq, sa)
 
 
@@ -165,29 +174,29 @@ class Qwen3DecoderLayer(nn.Module):
         hidden_states = self.mlp(hidden_states)
         return hidden_states, residual
 
-    def forward_fp8(self, positions: torch.Tensor, hidden_states: torch.Tensor | None,
-                    residual: torch.Tensor | None, tpf=None) -> tuple[torch.Tensor | None, torch.Tensor]:
-        """Fused FP8 layer. With tpf (utils.tp_fused.TpFused, tensor parallel) the
-        row-parallel GEMMs push their output rows to the ranks that own them and each
-        sum + add + RMSNorm + FP8 quantisation is one op; the layer then returns no
-        hidden state (the previous layer's output is in the peer buffers) and the
-        residual is current on this rank's rows."""
+    def forward_fp8(self, positions: torch.Tensor, hidden_states: torch.Tensor,
+                    residual: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Fused FP8 layer (one GPU, or tensor parallel with NCCL all-reduces)."""
         if residual is None:
             xq, sx, _ = self.input_layernorm.forward_fp8(hidden_states)
             residual = hidden_states
-        elif tpf is not None:
-            rows = residual.shape[0]
-            xq, sx = tpf.allreduce_norm_fp8(rows, residual, self.input_layernorm.weight, self.input_layernorm.eps,
-                                            pushed=True)
         else:
             xq, sx, residual = self.input_layernorm.forward_fp8(hidden_states, residual)
-        h = self.self_attn.forward_fp8(positions, xq, sx, tpf=tpf)
-        if tpf is not None:
-            xq, sx = tpf.allreduce_norm_fp8(residual.shape[0], residual, self.post_attention_layernorm.weight,
-                                            self.post_attention_layernorm.eps, pushed=True)
-        else:
-            xq, sx, residual = self.post_attention_layernorm.forward_fp8(h, residual)
-        return self.mlp.forward_fp8(xq, sx, tpf=tpf), residual
+        h = self.self_attn.forward_fp8(positions, xq, sx)
+        xq, sx, residual = self.post_attention_layernorm.forward_fp8(h, residual)
+        return self.mlp.forward_fp8(xq, sx), residual
+
+    def forward_tp(self, positions: torch.Tensor, xq: torch.Tensor, sx: torch.Tensor, residual: torch.Tensor,
+                   tpf, next_norm, final: bool):
+        """Fused FP8 layer, tensor parallel over peer memory (utils.tp_fused.TpFused):
+        xq/sx are this layer's normalised input rows; o_proj and down_proj each run as
+        one kernel with the all-reduce, the residual add (this rank's rows of
+        `residual`, updated in place) and the norm that follows them - the
+        post-attention norm, then `next_norm` (the next layer's input norm, or the
+        final norm when `final`, which returns fp16 rows instead of FP8 ones)."""
+        xq, sx = self.self_attn.forward_fp8(positions, xq, sx, tpf=tpf, norm=self.post_attention_layernorm,
+                                            residual=residual)
+        return self.mlp.forward_fp8(xq, sx, tpf=tpf, norm=next_norm, residual=residual, want_fp16=final)
 
 
 class Qwen3Model(nn.Module):
@@ -203,16 +212,26 @@ class Qwen3Model(nn.Module):
 
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         hidden_states = self.embed_tokens(input_ids)
-        residual = None
         fused = self._fp8_ready()
         tpf = getattr(self, "tp_fused", None) if fused else None
+        if tpf is not None:
+            # tensor parallel: the embedding rows are complete on every rank; from there on
+            # each row-parallel linear carries the all-reduce and the norm after it
+            residual = hidden_states
+            xq, sx, _ = self.layers[0].input_layernorm.forward_fp8(hidden_states)
+            last = len(self.layers) - 1
+            for i, layer in enumerate(self.layers):
+                nxt = self.norm if i == last else self.layers[i + 1].input_layernorm
+                out = layer.forward_tp(positions, xq, sx, residual, tpf, nxt, final=(i == last))
+                if i < last:
+                    xq, sx = out
+            return out
+        residual = None
         for layer in self.layers:
             if fused:
-                hidden_states, residual = layer.forward_fp8(positions, hidden_states, residual, tpf)
+                hidden_states, residual = layer.forward_fp8(positions, hidden_states, residual)
             else:
                 hidden_states, residual = layer(positions, hidden_states, residual)
-        if tpf is not None:
-            return tpf.allreduce_norm_fp16(residual.shape[0], residual, self.norm.weight, self.norm.eps, pushed=True)
         return self.norm(hidden_states, residual)[0]
 
 

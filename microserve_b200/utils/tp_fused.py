@@ -96,6 +96,22 @@ class TpFused:
             raise ValueError(f"TpFused holds {self.R} rows, {M} requested")
         kernels.fp8_gemm_rowpar(xq, sx, wq, sw, self.bases, self.rank, self.world, self.R)
 
+    def rowpar_gemm_norm(self, xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+                         residual: torch.Tensor, weight: torch.Tensor, eps: float, want_fp16: bool = False):
+        """Row-parallel FP8 GEMM + all-reduce + residual add + RMSNorm + FP8 quantisation as
+        one kernel (ms_fp8_gemm_rowpar_ar_rmsnorm): returns (xq [rows, H] e4m3, sx [rows]
+        fp32) of the normalised rows, or with want_fp16 the fp16 rows [rows, H]."""
+        from microserve_b200 import kernels
+        M, K = xq.shape
+        if wq.shape != (self.H, K):
+            raise ValueError(f"rowpar_gemm_norm: weight must be [{self.H}, {K}]")
+        self._check(M, residual)
+        kernels.fp8_gemm_rowpar_ar_rmsnorm(xq, sx, wq, sw, self.bases, self.rank, self.world, self.R, residual,
+                                           weight, eps, want_fp16)
+        if want_fp16:
+            return self._view("outh", torch.float16, (self.R, self.H))[:M]
+        return (self._view("outq", FP8, (self.R, self.H))[:M], self._view("outs", torch.float32, (self.R,))[:M])
+
     def allreduce_norm_fp8(self, rows: int, residual: torch.Tensor, weight: torch.Tensor, eps: float,
                            pushed: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
         """Sum the ranks' partial outputs (in `partial`, or already pushed by
@@ -113,11 +129,14 @@ class TpFused:
         self._launch(rows, residual, weight, eps, want_h=True, pushed=pushed)
         return self._view("outh", torch.float16, (self.R, self.H))[:rows]
 
-    def _launch(self, rows, residual, weight, eps, want_h, pushed):
+    def _check(self, rows, residual):
         if rows > self.R:
             raise ValueError(f"TpFused holds {self.R} rows, {rows} requested")
         if residual.shape != (rows, self.H) or residual.dtype != torch.float16 or not residual.is_contiguous():
             raise ValueError("residual must be a contiguous fp16 [rows, H] tensor")
+
+    def _launch(self, rows, residual, weight, eps, want_h, pushed):
+        self._check(rows, residual)
         check(_lib.load().ms_tp_allreduce_rmsnorm_fp8(self.bases, self.rank, self.world, self.H, self.R,
                                                       residual.data_ptr(), weight.data_ptr(), rows, float(eps),
                                                       1 if want_h else 0, 1 if pushed else 0, stream_ptr()),

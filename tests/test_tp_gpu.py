@@ -50,7 +50,7 @@ def _op_worker(rank, world, port, errq):
         from microserve_b200.utils import dist as tp
         from microserve_b200.utils.tp_fused import TpFused
         tp.init_tensor_parallel()
-        f = TpFused(256, H, torch.device("cuda", rank))
+        f = TpFused(1024, H, torch.device("cuda", rank))
         # several calls in a row: row counts change, fp16 and FP8 outputs alternate, and
         # the receive slots of both epoch parities are used and cleared
         for it, (rows, want_h) in enumerate(((64, False), (37, False), (64, True), (1, False), (64, False),
@@ -123,6 +123,38 @@ def _op_worker(rank, world, port, errq):
             o_part = [O.fp8_gemm(*[t.cpu() for t in sh]).float() for sh in shards]
             o_y, _ = O.rmsnorm(torch.stack(o_part).sum(0).half(), nw.cpu(), 1e-6, residual)
             assert O.rel_l2(ky.cpu(), o_y) < 2e-3, f"pushed GEMM vs oracle, case {it}"
+        assert _lib.device_status() == 0
+
+        # the same as ONE kernel (ms_fp8_gemm_rowpar_ar_rmsnorm: the GEMM's CTAs do the row work
+        # after pushing their tiles), and its fallback to GEMM + op for prefill-sized M (600 rows)
+        for it, (rows, k_shard, want_h) in enumerate(((256, 512, False), (1, 512, False), (37, 1536, True),
+                                                      (200, 1536, False), (256, 6144, False), (64, 4096, False),
+                                                      (600, 512, False), (256, 768, True))):
+            g = torch.Generator().manual_seed(500 + it)
+            x = torch.randn(rows, world * k_shard, generator=g).half()
+            w = (torch.randn(H, world * k_shard, generator=g) * 0.02).half()
+            shards = []
+            for p in range(world):
+                xq_p, sx_p = O.quantize_rows(x[:, p * k_shard:(p + 1) * k_shard])
+                wq_p, sw_p = O.quantize_weight(w[:, p * k_shard:(p + 1) * k_shard])
+                shards.append([t.cuda() for t in (xq_p, sx_p, wq_p, sw_p)])
+            residual = torch.randn(rows, H, generator=g).half()
+            nw = (1 + 0.1 * torch.randn(H, generator=g)).half().cuda()
+            res = residual.cuda()
+            out = f.rowpar_gemm_norm(*shards[rank], res, nw, 1e-6, want_fp16=want_h)
+            torch.cuda.synchronize()
+            parts = [kernels.fp8_gemm(*sh).float() for sh in shards]
+            total = torch.stack(parts).sum(0).half()
+            ky, kq, ks, kr = kernels.rmsnorm(total, nw, 1e-6, residual.cuda(), want_fp16=True, want_fp8=True)
+            R = (rows + world - 1) // world
+            own = slice(rank * R, min(rows, (rank + 1) * R))
+            assert torch.equal(res[own], kr[own]), f"one-kernel row-parallel op: residual rows, case {it}"
+            if want_h:
+                assert torch.equal(out, ky), f"one-kernel row-parallel op: fp16 rows, case {it}"
+            else:
+                q, s = out
+                assert torch.equal(s, ks) and torch.equal(q.view(torch.uint8), kq.view(torch.uint8)), \
+                    f"one-kernel row-parallel op: codes / scales, case {it}"
         assert _lib.device_status() == 0
 
         # exact activation scales: shard k of a full row quantised with the global row amax
