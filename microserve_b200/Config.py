@@ -6,6 +6,11 @@
                          row-parallel outputs with this library's peer-memory
                          kernel fused with add + RMSNorm + FP8 quantisation
                          (utils/tp_fused.py) instead of NCCL all-reduce;
+  tp_fused_gemm        - with the fused collective: each row-parallel GEMM
+                         pushes its rows to their owners and does the
+                         reduce / norm itself (one kernel); False: the GEMM
+                         writes its partial locally and a second kernel does
+                         the rest;
   tp_exact_act_scale   - with tensor parallelism, scale each row-parallel
                          input row (o_proj, down_proj) by its amax over the
                          full row, as a single GPU does (one all-reduce max of
@@ -44,6 +49,7 @@ class Config:
     scheduler_policy: str = "mixed"
     tensor_parallel_size: int = 1
     tp_fused_collective: bool = True
+    tp_fused_gemm: bool = True
     tp_exact_act_scale: bool = False
     load_format: str = "safetensors"
     hf_config: object = None

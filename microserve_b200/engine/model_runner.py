@@ -124,7 +124,7 @@ class ModelRunner:
                 and config.kv_cache_dtype == "fp8_e4m3"):
             from microserve_b200.utils.tp_fused import TpFused
             rows = max(config.max_num_batched_tokens, (config.max_num_seqs + 15) // 16 * 16)
-            self.tp_fused = TpFused(rows, hf.hidden_size, self.device)
+            self.tp_fused = TpFused(rows, hf.hidden_size, self.device, fused_gemm=config.tp_fused_gemm)
             self.model.model.tp_fused = self.tp_fused
         torch.cuda.empty_cache()
 

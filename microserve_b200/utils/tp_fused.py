@@ -37,7 +37,8 @@ def layout(world: int, hidden: int, max_rows: int) -> dict[str, int]:
 
 
 class TpFused:
-    def __init__(self, max_rows: int, hidden: int, device: torch.device):
+    def __init__(self, max_rows: int, hidden: int, device: torch.device, fused_gemm: bool = True):
+        self.fused_gemm = fused_gemm
         self.world, self.rank = tp.tp_size(), tp.tp_rank()
         if not 1 < self.world <= 8:
             raise ValueError("TpFused needs 2..8 ranks")
@@ -98,14 +99,21 @@ class TpFused:
 
     def rowpar_gemm_norm(self, xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
                          residual: torch.Tensor, weight: torch.Tensor, eps: float, want_fp16: bool = False):
-        """Row-parallel FP8 GEMM + all-reduce + residual add + RMSNorm + FP8 quantisation as
-        one kernel (ms_fp8_gemm_rowpar_ar_rmsnorm): returns (xq [rows, H] e4m3, sx [rows]
-        fp32) of the normalised rows, or with want_fp16 the fp16 rows [rows, H]."""
+        """Row-parallel FP8 GEMM + all-reduce + residual add + RMSNorm + FP8 quantisation:
+        returns (xq [rows, H] e4m3, sx [rows] fp32) of the normalised rows, or with
+        want_fp16 the fp16 rows [rows, H]. With fused_gemm one kernel
+        (ms_fp8_gemm_rowpar_ar_rmsnorm); otherwise the GEMM writes this rank's partial
+        output locally and ms_tp_allreduce_rmsnorm_fp8 does the rest."""
         from microserve_b200 import kernels
         M, K = xq.shape
         if wq.shape != (self.H, K):
             raise ValueError(f"rowpar_gemm_norm: weight must be [{self.H}, {K}]")
         self._check(M, residual)
+        if not self.fused_gemm:
+            kernels.fp8_gemm(xq, sx, wq, sw, out=self.partial(M))
+            if want_fp16:
+                return self.allreduce_norm_fp16(M, residual, weight, eps)
+            return self.allreduce_norm_fp8(M, residual, weight, eps)
         kernels.fp8_gemm_rowpar_ar_rmsnorm(xq, sx, wq, sw, self.bases, self.rank, self.world, self.R, residual,
                                            weight, eps, want_fp16)
         if want_fp16:
