@@ -167,7 +167,7 @@ def build_engine(args, cfg, max_model_len):
                             tensor_parallel_size=args.gpus, gpu_memory_utilization=0.9, seed=0,
                             num_kvcache_blocks=args.kv_blocks,
                             tp_fused_collective=not getattr(args, "nccl_allreduce", False),
-                            tp_fused_gemm=not getattr(args, "tp_two_kernels", False),
+                            tp_fused_gemm=getattr(args, "tp_one_kernel", False),
                             tp_exact_act_scale=getattr(args, "exact_act_scale", False)))
 
 
@@ -562,8 +562,8 @@ def run_ours(args):
                   "tp_collective": ("nccl all-reduce" if args.nccl_allreduce else
                                     "fused peer-memory all-reduce+rmsnorm+fp8") if args.gpus > 1 else None,
                   "tp_act_scale": "exact (full row)" if args.exact_act_scale else "per shard",
-                  "tp_row_parallel": ("GEMM + separate reduce/norm op" if args.tp_two_kernels else
-                                      "one kernel: GEMM pushing rows + reduce/norm tail") if args.gpus > 1 else None},
+                  "tp_row_parallel": ("one kernel: GEMM pushing rows + reduce/norm tail" if args.tp_one_kernel else
+                                      "GEMM + separate reduce/norm op") if args.gpus > 1 else None},
         "roofline": dict(roof, peak_kind=f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s"),
         "kernels": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in v.items()
@@ -978,8 +978,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nccl-allreduce", action="store_true",
                     help="tensor parallel: NCCL all-reduce instead of the fused peer-memory kernel")
-    ap.add_argument("--tp-two-kernels", action="store_true",
-                    help="tensor parallel: row-parallel GEMM writing locally + the separate reduce/norm op")
+    ap.add_argument("--tp-one-kernel", action="store_true",
+                    help="tensor parallel: row-parallel GEMM pushing its rows + reduce/norm tail, one kernel")
     ap.add_argument("--exact-act-scale", action="store_true",
                     help="tensor parallel: row-parallel activation scales from the full row (all-reduce max)")
     ap.add_argument("--no-pdl", action="store_true",

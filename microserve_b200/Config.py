@@ -49,7 +49,7 @@ class Config:
     scheduler_policy: str = "mixed"
     tensor_parallel_size: int = 1
     tp_fused_collective: bool = True
-    tp_fused_gemm: bool = True
+    tp_fused_gemm: bool = False
     tp_exact_act_scale: bool = False
     load_format: str = "safetensors"
     hf_config: object = None
