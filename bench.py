@@ -605,6 +605,10 @@ def time_decode_steps(engine, batch, args, lib, local, sample_clocks=True):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with (ClockSampler(local) if sample_clocks else _NoClocks()) as clocks:
+        # every rank's sampler is running before any rank starts its clock: a rank that
+        # entered the region early would wait in its first step for its peers (each
+        # tensor-parallel step synchronises the ranks) and count that wait
+        sync_all()
         torch.cuda.nvtx.range_push("decode_timed")
         clocks.mark_start()
         start.record()

@@ -667,6 +667,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = c_first; c <= c_last; ++c) args.flags[c] = 0;
       }
     }
+    // With the tensor-parallel tail the peers poll for the rows pushed above while this
+    // kernel still runs: make them performed now instead of at the kernel's end (plain
+    // stores to a peer may otherwise wait in the write path; measured ~14 us per call).
+    if (args.rp_tail) __threadfence_system();
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
