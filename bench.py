@@ -960,10 +960,23 @@ def run_kernel(args):
             t = time_kernel(launch, iters=args.steps, warm=args.warmup)
             byts = N * K + M * K + 2 * M * N + 4 * (M + N)
             flops = 2 * M * N * K
-            print(json.dumps({"kernel": "fp8_gemm", "impl": args.impl, "M": M, "N": N, "K": K,
-                              "us": round(t * 1e6, 2),
-                              "GBps": round(byts / t / 1e9, 1), "frac_hbm": round(byts / t / 1e9 / hbm_peak, 4),
-                              "TFLOPs": round(flops / t / 1e12, 1)}), flush=True)
+            line = {"kernel": "fp8_gemm", "impl": args.impl, "M": M, "N": N, "K": K, "us": round(t * 1e6, 2),
+                    "GBps": round(byts / t / 1e9, 1), "frac_hbm": round(byts / t / 1e9 / hbm_peak, 4),
+                    "TFLOPs": round(flops / t / 1e12, 1)}
+            if ref is None:
+                # the library bar: cuBLAS FP8 GEMM (torch._scaled_mm, one scale per tensor, so
+                # less epilogue work than the per-row x per-channel dequantisation above)
+                one = torch.ones((), device=dev)
+
+                def cublas():
+                    torch._scaled_mm(xq, wqs[it[0] % copies].t(), scale_a=one, scale_b=one, out_dtype=torch.float16)
+                    it[0] += 1
+                try:
+                    line["cublas_scaled_mm_us"] = round(time_kernel(cublas, iters=args.steps, warm=args.warmup) * 1e6, 2)
+                except RuntimeError as e:  # a shape cuBLAS does not take (K or N not a multiple of 16)
+                    line["cublas_scaled_mm_us"] = None
+                    line["cublas_error"] = str(e).splitlines()[0][:120]
+            print(json.dumps(line), flush=True)
 
 
 def main():

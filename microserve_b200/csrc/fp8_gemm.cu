@@ -140,7 +140,7 @@ __device__ __forceinline__ void tma_store_2d_wait(const CUtensorMap* map, uint32
 // The tensor-parallel row work at the end of a row-parallel GEMM (rp_tail): runs on
 // all threads of the CTA once its tiles are pushed; the stage buffers are free by
 // then and hold the staged row (smem >= H * 2 + 256 bytes).
-template <int NVT>
+template <int NVT, int WB>
 __device__ __noinline__ void rowpar_tail(const TpRows& a, unsigned char* smem) {
   H8* srow = reinterpret_cast<H8*>(smem);
   float* red_ss = reinterpret_cast<float*>(smem + a.H * 2);
@@ -153,8 +153,8 @@ __device__ __noinline__ void rowpar_tail(const TpRows& a, unsigned char* smem) {
   const uint64_t limit = wait_limit_ns();
   bool fail = false;
   for (int j = blockIdx.x; j < a.R && !fail; j += gridDim.x)
-    if (a.rank * a.R + j < a.M) fail = !tp_reduce_row<NVT>(a, j, b, limit, srow, red_ss, red_max);
-  for (int j = blockIdx.x; j < a.R && !fail; j += gridDim.x) fail = !tp_collect_rows(a, j, b, limit);
+    if (a.rank * a.R + j < a.M) fail = !tp_reduce_row<NVT, WB>(a, j, b, limit, srow, red_ss, red_max);
+  for (int j = blockIdx.x; j < a.R && !fail; j += gridDim.x) fail = !tp_collect_rows<NVT, WB>(a, j, b, limit);
   fail = __syncthreads_or(fail) != 0;
   if (threadIdx.x == 0) tp_finish_call(a, fail, e);
 }
@@ -494,6 +494,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           unsigned char* sa = smem + s * C::kStageBytes;
           mbar_arrive_expect_tx(&full[s], C::kStageBytes);
           // weights never depend on the preceding grid: stream them before waiting for it
+          // (requesting every free stage's weights before the wait measured slower: the
+          // first stage's activations then queue behind them)
           load_stage<CH>(&tmap_w, smem_u32(sa), &full[s], k, n0);
           if (!waited) {
             pdl_wait();
@@ -667,10 +669,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = c_first; c <= c_last; ++c) args.flags[c] = 0;
       }
     }
-    // With the tensor-parallel tail the peers poll for the rows pushed above while this
-    // kernel still runs: make them performed now instead of at the kernel's end (plain
-    // stores to a peer may otherwise wait in the write path; measured ~14 us per call).
-    if (args.rp_tail) __threadfence_system();
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -681,12 +679,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (args.rp_tail) {  // this CTA's tiles are all pushed: its share of the row work
     __syncwarp();
-    switch (args.rp_nvt) {
-      case 1: rowpar_tail<1>(args.tail, smem); break;
-      case 2: rowpar_tail<2>(args.tail, smem); break;
-      case 3: rowpar_tail<3>(args.tail, smem); break;
-      default: rowpar_tail<4>(args.tail, smem); break;
-    }
+    const int wb = tp_world_bound(args.tail.world);
+#define MS_TAIL(N, W) \
+  if (args.rp_nvt == N && wb == W) rowpar_tail<N, W>(args.tail, smem);
+    MS_TAIL(1, 2) MS_TAIL(1, 4) MS_TAIL(1, 8)
+    MS_TAIL(2, 2) MS_TAIL(2, 4) MS_TAIL(2, 8)
+    MS_TAIL(3, 2) MS_TAIL(3, 4) MS_TAIL(3, 8)
+    MS_TAIL(4, 2) MS_TAIL(4, 4) MS_TAIL(4, 8)
+#undef MS_TAIL
   }
 }
 

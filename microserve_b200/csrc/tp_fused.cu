@@ -19,11 +19,12 @@ constexpr int kTpThreads = 512;
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
-// NVT: 16-byte vectors of an fp16 row per thread (ceil(H / 8 / blockDim)). The grid
+// NVT: 16-byte vectors of an fp16 row per thread (ceil(H / 8 / blockDim)); WB: a
+// bound on the ranks (2, 4 or 8) that sizes the loads kept in flight. The grid
 // has at most one CTA per SM, so every CTA of every rank is resident at once; CTA c
 // handles the row indices j = c, c + gridDim, ... < R and issues all of its pushes
 // before its first wait.
-template <int NVT>
+template <int NVT, int WB>
 __global__ void __launch_bounds__(kTpThreads) tp_rowpar_norm_kernel(TpRows a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];  // the owned row after the residual add, [H] fp16
   H8* srow = reinterpret_cast<H8*>(smem_raw);
@@ -38,8 +39,8 @@ __global__ void __launch_bounds__(kTpThreads) tp_rowpar_norm_kernel(TpRows a) {
     for (int j = blockIdx.x; j < a.R; j += gridDim.x) tp_push_rows(a, j, b);
   bool fail = false;
   for (int j = blockIdx.x; j < a.R && !fail; j += gridDim.x)
-    if (a.rank * a.R + j < a.M) fail = !tp_reduce_row<NVT>(a, j, b, limit, srow, red_ss, red_max);
-  for (int j = blockIdx.x; j < a.R && !fail; j += gridDim.x) fail = !tp_collect_rows(a, j, b, limit);
+    if (a.rank * a.R + j < a.M) fail = !tp_reduce_row<NVT, WB>(a, j, b, limit, srow, red_ss, red_max);
+  for (int j = blockIdx.x; j < a.R && !fail; j += gridDim.x) fail = !tp_collect_rows<NVT, WB>(a, j, b, limit);
   fail = __syncthreads_or(fail) != 0;
   if (threadIdx.x == 0) tp_finish_call(a, fail, e);
 }
@@ -130,13 +131,16 @@ cudaError_t launch_tp_allreduce_rmsnorm_fp8(void* const* bases, int rank, int wo
   // precede it): every CTA of every rank is then resident at once, whatever the
   // order in which the hardware dispatches them
   const dim3 grid(a.R < num_sms ? a.R : num_sms);
-  switch (nvt) {
-    case 1: return launch_kernel(tp_rowpar_norm_kernel<1>, grid, dim3(T), smem, stream, a);
-    case 2: return launch_kernel(tp_rowpar_norm_kernel<2>, grid, dim3(T), smem, stream, a);
-    case 3: return launch_kernel(tp_rowpar_norm_kernel<3>, grid, dim3(T), smem, stream, a);
-    case 4: return launch_kernel(tp_rowpar_norm_kernel<4>, grid, dim3(T), smem, stream, a);
-    default: return cudaErrorInvalidValue;
-  }
+  const int wb = tp_world_bound(world);
+#define MS_TP_OP(N, W)                   \
+  if (nvt == N && wb == W)               \
+    return launch_kernel(tp_rowpar_norm_kernel<N, W>, grid, dim3(T), smem, stream, a);
+  MS_TP_OP(1, 2) MS_TP_OP(1, 4) MS_TP_OP(1, 8)
+  MS_TP_OP(2, 2) MS_TP_OP(2, 4) MS_TP_OP(2, 8)
+  MS_TP_OP(3, 2) MS_TP_OP(3, 4) MS_TP_OP(3, 8)
+  MS_TP_OP(4, 2) MS_TP_OP(4, 4) MS_TP_OP(4, 8)
+#undef MS_TP_OP
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace ms

@@ -106,16 +106,22 @@ __device__ __forceinline__ uint4 tp_unpattern16(uint4 v) {
   return make_uint4(tp_unpattern16(v.x), tp_unpattern16(v.y), tp_unpattern16(v.z), tp_unpattern16(v.w));
 }
 
-// Re-reads *p until `v` has no pending element; false after `limit` ns.
+// Re-reads *p until no element is pending and returns the vector; after `limit` ns it
+// returns the last read, still pending. (Returned by value: a vector passed by
+// reference would live in local memory, and storing each load's result there would
+// serialise the loads that should be in flight together.)
 template <bool kCodes>
-__device__ __noinline__ bool tp_poll_v4(const void* p, uint4& v, uint64_t limit) {
+__device__ __noinline__ uint4 tp_poll_v4(const void* p, uint64_t limit) {
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
-    v = tp_ld_volatile_v4(p);
-    if (!(kCodes ? tp_pending8(v) : tp_pending16(v))) return true;
-    if ((i & 63u) == 0 && global_ns() - t0 > limit) return false;
+    const uint4 v = tp_ld_volatile_v4(p);
+    if (!(kCodes ? tp_pending8(v) : tp_pending16(v))) return v;
+    if ((i & 63u) == 0 && global_ns() - t0 > limit) return v;
   }
 }
+
+// The compile-time bound on the ranks that the row work is instantiated for.
+__host__ __device__ constexpr int tp_world_bound(int world) { return world <= 2 ? 2 : world <= 4 ? 4 : 8; }
 
 // Host: the arguments for one call (pointers from every rank's buffer base, sizes);
 // residual, weight, eps, want_h and pushed are left for the caller.
@@ -146,62 +152,90 @@ __device__ __forceinline__ void tp_push_rows(const TpRows& a, int j, int b) {
   }
 }
 
+// Vectors a thread keeps in flight at once in reduce and collect: the row's
+// vectors are taken in groups of kI (NVT per thread in all, WB parts or peers
+// each), and every load of a group is issued before the first one is used, so a
+// group costs one memory round trip instead of one per vector (at most 16
+// vectors, 64 registers).
+template <int NVT, int WB>
+struct TpGroup {
+  static constexpr int kI = (16 / WB) < NVT ? (16 / WB) : NVT;
+};
+
 // reduce: the owned row rank R + j (all threads of the CTA; srow: the row, [H] fp16
-// in shared memory; red_ss >= kMaxRowWarps floats, red_max >= 32 floats). Returns
-// false if a part did not arrive within the wait limit (CTA-uniform).
-template <int NVT>
+// in shared memory; red_ss >= kMaxRowWarps floats, red_max >= 32 floats). WB >=
+// world. Returns false if a part did not arrive within the wait limit
+// (CTA-uniform).
+template <int NVT, int WB>
 __device__ __forceinline__ bool tp_reduce_row(const TpRows& a, int j, int b, uint64_t limit, H8* srow,
                                               float* red_ss, float* red_max) {
+  constexpr int kI = TpGroup<NVT, WB>::kI;
   const int t = threadIdx.x, T = blockDim.x;
   const int H = a.H, nv = H / 8;
   const int64_t m0 = (int64_t)a.rank * a.R + j;
   bool fail = false;
   H8 rn[NVT];
 #pragma unroll
-  for (int i = 0; i < NVT; ++i) {
-    const int c = t + i * T;
-    if (c >= nv) continue;
-    uint4 x[kTpMaxWorld];
+  for (int g = 0; g < NVT; g += kI) {
+    uint4 x[kI][WB];
+    H8 r[kI];
 #pragma unroll
-    for (int p = 0; p < kTpMaxWorld; ++p) {
-      if (p >= a.world) continue;
-      x[p] = (p == a.rank && !a.pushed) ? __ldcg(reinterpret_cast<const uint4*>(a.partial + m0 * H) + c)
-                                        : tp_ld_volatile_v4(tp_slot(a, a.rank, b, p, j) + 8 * c);
+    for (int i = 0; i < kI; ++i) {  // the group's loads: every part and the residual
+      const int c = t + (g + i) * T;
+      if (g + i >= NVT || c >= nv) continue;
+#pragma unroll
+      for (int p = 0; p < WB; ++p) {
+        if (p >= a.world) continue;
+        x[i][p] = (p == a.rank && !a.pushed) ? __ldcg(reinterpret_cast<const uint4*>(a.partial + m0 * H) + c)
+                                             : tp_ld_volatile_v4(tp_slot(a, a.rank, b, p, j) + 8 * c);
+      }
+      r[i] = ld_h8(a.residual + m0 * H + 8 * c);
     }
 #pragma unroll
-    for (int p = 0; p < kTpMaxWorld; ++p)
-      if (p < a.world && (p != a.rank || a.pushed) && !fail && tp_pending16(x[p]))
-        fail = !tp_poll_v4<false>(tp_slot(a, a.rank, b, p, j) + 8 * c, x[p], limit);
-    float acc[8];
+    for (int i = 0; i < kI; ++i) {  // parts not yet written: wait for them
+      const int c = t + (g + i) * T;
+      if (g + i >= NVT || c >= nv) continue;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+      for (int p = 0; p < WB; ++p)
+        if (p < a.world && (p != a.rank || a.pushed) && !fail && tp_pending16(x[i][p])) {
+          x[i][p] = tp_poll_v4<false>(tp_slot(a, a.rank, b, p, j) + 8 * c, limit);
+          fail = tp_pending16(x[i][p]);
+        }
+    }
 #pragma unroll
-    for (int p = 0; p < kTpMaxWorld; ++p) {
-      if (p >= a.world) continue;
-      const H8 h = as_h8(x[p]);
+    for (int i = 0; i < kI; ++i) {
+      const int c = t + (g + i) * T;
+      if (g + i >= NVT || c >= nv) continue;
+      float acc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+#pragma unroll
+      for (int p = 0; p < WB; ++p) {  // rank order
+        if (p >= a.world) continue;
+        const H8 h = as_h8(x[i][p]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(h.h[k]);
+          acc[2 * k] += f.x;
+          acc[2 * k + 1] += f.y;
+        }
+      }
+      // the slots are read: back to "not yet written" for the call after next
+#pragma unroll
+      for (int p = 0; p < WB; ++p)
+        if (p < a.world && (p != a.rank || a.pushed))
+          *reinterpret_cast<uint4*>(tp_slot(a, a.rank, b, p, j) + 8 * c) = tp_pattern4();
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const float2 f = __half22float2(h.h[k]);
-        acc[2 * k] += f.x;
-        acc[2 * k + 1] += f.y;
+        const float2 fr = __half22float2(r[i].h[k]);
+        const float x0 = __half2float(__float2half_rn(acc[2 * k]));
+        const float x1 = __half2float(__float2half_rn(acc[2 * k + 1]));
+        r[i].h[k] = __floats2half2_rn(x0 + fr.x, x1 + fr.y);
       }
+      if (!fail) st_h8(a.residual + m0 * H + 8 * c, r[i]);
+      rn[g + i] = r[i];
+      srow[c] = r[i];
     }
-    // the slots are read: back to "not yet written" for the call after next
-#pragma unroll
-    for (int p = 0; p < kTpMaxWorld; ++p)
-      if (p < a.world && (p != a.rank || a.pushed))
-        *reinterpret_cast<uint4*>(tp_slot(a, a.rank, b, p, j) + 8 * c) = tp_pattern4();
-    H8 r = ld_h8(a.residual + m0 * H + 8 * c);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 fr = __half22float2(r.h[k]);
-      const float x0 = __half2float(__float2half_rn(acc[2 * k]));
-      const float x1 = __half2float(__float2half_rn(acc[2 * k + 1]));
-      r.h[k] = __floats2half2_rn(x0 + fr.x, x1 + fr.y);
-    }
-    if (!fail) st_h8(a.residual + m0 * H + 8 * c, r);
-    rn[i] = r;
-    srow[c] = r;
   }
   if (__syncthreads_or(fail)) return false;
 
@@ -236,14 +270,14 @@ __device__ __forceinline__ bool tp_reduce_row(const TpRows& a, int j, int b, uin
       const uint4 yh = tp_unpattern16(as_u4(rn[i]));
       *reinterpret_cast<uint4*>(a.outh + m0 * H + 8 * c) = yh;
 #pragma unroll
-      for (int p = 0; p < kTpMaxWorld; ++p)
+      for (int p = 0; p < WB; ++p)
         if (p < a.world && p != a.rank) tp_st_volatile_v4(a.grh[p] + gslot * H + 8 * c, yh);
     } else {
       uint2 q = encode8(rn[i], scale, rcp);
       q = make_uint2(tp_unpattern8(q.x), tp_unpattern8(q.y));
       *reinterpret_cast<uint2*>(a.outq + m0 * H + 8 * c) = q;
 #pragma unroll
-      for (int p = 0; p < kTpMaxWorld; ++p)
+      for (int p = 0; p < WB; ++p)
         if (p < a.world && p != a.rank) tp_st_volatile_v2(a.grq[p] + gslot * H + 8 * c, q);
     }
   }
@@ -256,40 +290,73 @@ __device__ __forceinline__ bool tp_reduce_row(const TpRows& a, int j, int b, uin
 }
 
 // collect: rows p R + j of the other owners, from this rank's gather slots into its
-// output (the slots are reset after reading). Returns false on a timeout.
+// output (the slots are reset after reading): every peer's vectors of a group are
+// loaded at once, and thread p waits for peer p's scale. WB >= world. Returns
+// false on a timeout.
+template <int NVT, int WB>
 __device__ __forceinline__ bool tp_collect_rows(const TpRows& a, int j, int b, uint64_t limit) {
+  constexpr int kI = TpGroup<NVT, WB>::kI;
   const int t = threadIdx.x, T = blockDim.x;
   const int64_t H = a.H;
   const int me = a.rank;
-  for (int p = 0; p < a.world; ++p) {
-    const int64_t m = (int64_t)p * a.R + j;
-    if (p == me || m >= a.M) continue;
-    const int64_t gslot = (int64_t)b * a.g_half + m;
-    if (a.want_h) {
-      for (int c = t; c < H / 8; c += T) {
-        __half* src = a.grh[me] + gslot * H + 8 * c;
-        uint4 v = tp_ld_volatile_v4(src);
-        if (tp_pending16(v) && !tp_poll_v4<false>(src, v, limit)) return false;
-        *reinterpret_cast<uint4*>(a.outh + m * H + 8 * c) = v;
-        *reinterpret_cast<uint4*>(src) = tp_pattern4();
+  const int nvec = a.want_h ? (int)(H / 8) : (int)(H / 16);  // 16-byte vectors of a gathered row
+  const size_t vbytes = a.want_h ? (size_t)H * 2 : (size_t)H;
+  unsigned char* const slots = a.want_h ? reinterpret_cast<unsigned char*>(a.grh[me]) : a.grq[me];
+  unsigned char* const out = a.want_h ? reinterpret_cast<unsigned char*>(a.outh) : a.outq;
+  bool fail = false;
+#pragma unroll
+  for (int g = 0; g < NVT; g += kI) {
+    uint4 v[kI][WB];
+#pragma unroll
+    for (int i = 0; i < kI; ++i) {
+      const int c = t + (g + i) * T;
+      if (g + i >= NVT || c >= nvec) continue;
+#pragma unroll
+      for (int p = 0; p < WB; ++p) {
+        const int64_t m = (int64_t)p * a.R + j;
+        if (p >= a.world || p == me || m >= a.M) continue;
+        v[i][p] = tp_ld_volatile_v4(slots + ((int64_t)b * a.g_half + m) * vbytes + 16 * c);
       }
-    } else {
-      for (int c = t; c < H / 16; c += T) {
-        uint8_t* src = a.grq[me] + gslot * H + 16 * c;
-        uint4 v = tp_ld_volatile_v4(src);
-        if (tp_pending8(v) && !tp_poll_v4<true>(src, v, limit)) return false;
-        *reinterpret_cast<uint4*>(a.outq + m * H + 16 * c) = v;
-        *reinterpret_cast<uint4*>(src) = tp_pattern4();
+    }
+#pragma unroll
+    for (int i = 0; i < kI; ++i) {
+      const int c = t + (g + i) * T;
+      if (g + i >= NVT || c >= nvec) continue;
+#pragma unroll
+      for (int p = 0; p < WB; ++p) {
+        const int64_t m = (int64_t)p * a.R + j;
+        if (p >= a.world || p == me || m >= a.M || fail) continue;
+        unsigned char* src = slots + ((int64_t)b * a.g_half + m) * vbytes + 16 * c;
+        if (a.want_h ? tp_pending16(v[i][p]) : tp_pending8(v[i][p])) {
+          v[i][p] = a.want_h ? tp_poll_v4<false>(src, limit) : tp_poll_v4<true>(src, limit);
+          fail = a.want_h ? tp_pending16(v[i][p]) : tp_pending8(v[i][p]);
+        }
       }
-      if (t == 0) {
-        float* sp = a.grs[me] + gslot;
-        const uint64_t t0 = global_ns();
-        uint32_t v;
-        for (uint32_t i = 1; (v = tp_ld_volatile_u32(sp)) == kTpPattern; ++i)
-          if ((i & 63u) == 0 && global_ns() - t0 > limit) return false;
-        a.outs[m] = __uint_as_float(v);
-        *reinterpret_cast<uint32_t*>(sp) = kTpPattern;
+    }
+    if (fail) return false;
+#pragma unroll
+    for (int i = 0; i < kI; ++i) {
+      const int c = t + (g + i) * T;
+      if (g + i >= NVT || c >= nvec) continue;
+#pragma unroll
+      for (int p = 0; p < WB; ++p) {
+        const int64_t m = (int64_t)p * a.R + j;
+        if (p >= a.world || p == me || m >= a.M) continue;
+        *reinterpret_cast<uint4*>(out + m * vbytes + 16 * c) = v[i][p];
+        *reinterpret_cast<uint4*>(slots + ((int64_t)b * a.g_half + m) * vbytes + 16 * c) = tp_pattern4();
       }
+    }
+  }
+  if (!a.want_h && t < a.world && t != me) {  // thread p: peer p's scale
+    const int64_t m = (int64_t)t * a.R + j;
+    if (m < a.M) {
+      float* sp = a.grs[me] + (int64_t)b * a.g_half + m;
+      const uint64_t t0 = global_ns();
+      uint32_t v;
+      for (uint32_t i = 1; (v = tp_ld_volatile_u32(sp)) == kTpPattern; ++i)
+        if ((i & 63u) == 0 && global_ns() - t0 > limit) return false;
+      a.outs[m] = __uint_as_float(v);
+      *reinterpret_cast<uint32_t*>(sp) = kTpPattern;
     }
   }
   return true;
