@@ -13,6 +13,7 @@ _GROUP = None
 _RANK = 0
 _SIZE = 1
 _EXACT_ACT_SCALE = False
+_ORDERED_SUM = False
 
 
 def init_tensor_parallel(group=None) -> None:
@@ -26,8 +27,17 @@ def init_tensor_parallel(group=None) -> None:
 
 
 def reset_tensor_parallel() -> None:
-    global _GROUP, _RANK, _SIZE, _EXACT_ACT_SCALE
-    _GROUP, _RANK, _SIZE, _EXACT_ACT_SCALE = None, 0, 1, False
+    global _GROUP, _RANK, _SIZE, _EXACT_ACT_SCALE, _ORDERED_SUM
+    _GROUP, _RANK, _SIZE, _EXACT_ACT_SCALE, _ORDERED_SUM = None, 0, 1, False, False
+
+
+def set_ordered_sum(enable: bool) -> None:
+    """For checks: all_reduce_ of fp16 tensors as an all-gather and an fp32 sum in rank
+    order, rounded to fp16 once - the arithmetic of the fused peer-memory collective -
+    instead of NCCL's reduction, whose order and intermediate fp16 roundings depend on
+    the algorithm it picks (identical to it for two ranks, where a + b = b + a)."""
+    global _ORDERED_SUM
+    _ORDERED_SUM = bool(enable)
 
 
 def set_exact_act_scale(enable: bool) -> None:
@@ -57,7 +67,15 @@ def tp_group():
 def all_reduce_(x: torch.Tensor) -> torch.Tensor:
     """In-place sum over the TP group (identity when tp_size == 1)."""
     if _SIZE > 1:
-        dist.all_reduce(x, group=_GROUP)
+        if _ORDERED_SUM and x.dtype == torch.float16:
+            parts = [torch.empty_like(x, memory_format=torch.contiguous_format) for _ in range(_SIZE)]
+            dist.all_gather(parts, x.contiguous(), group=_GROUP)
+            acc = parts[0].float()
+            for part in parts[1:]:
+                acc += part.float()
+            x.copy_(acc.half())
+        else:
+            dist.all_reduce(x, group=_GROUP)
     return x
 
 

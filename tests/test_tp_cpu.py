@@ -89,3 +89,47 @@ def test_tensor_parallel_layers_two_gloo_ranks(tmp_path):
         errs.append(errq.get())
     assert not errs, "\n".join(errs)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+def _ordered_sum_worker(rank, world, init_file, errq):
+    try:
+        dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
+        from microserve_b200.utils import dist as tp
+        tp.init_tensor_parallel()
+        parts = [(torch.randn(3, 40, generator=torch.Generator().manual_seed(p)) * 10 ** p).half()
+                 for p in range(world)]
+        acc = torch.zeros(3, 40)
+        for p in range(world):  # fp32, rank order, one rounding at the end
+            acc = acc + parts[p].float()
+        x = parts[rank].clone()
+        tp.set_ordered_sum(True)
+        assert tp.all_reduce_(x) is x
+        assert torch.equal(x, acc.half())
+        tp.set_ordered_sum(False)
+        y = tp.all_reduce_(torch.ones(4, dtype=torch.float32))  # other dtypes: the plain all-reduce
+        assert torch.equal(y, torch.full((4,), float(world)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as ex:
+        import traceback
+        errq.put(f"rank {rank}: {ex}\n{traceback.format_exc()}")
+        raise
+    os._exit(0)
+
+
+def test_ordered_sum_is_the_rank_order_fp32_sum_four_gloo_ranks(tmp_path):
+    """The reference all-reduce of bench.py's tensor-parallel parity check: an fp32 sum in
+    rank order rounded to fp16 once, on every rank (4 ranks, magnitudes 1..1000 so that
+    another order would round differently)."""
+    ctx = mp.get_context("spawn")
+    errq = ctx.Queue()
+    procs = [ctx.Process(target=_ordered_sum_worker, args=(r, 4, str(tmp_path / "pg"), errq)) for r in range(4)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not errs, "\n".join(errs)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]

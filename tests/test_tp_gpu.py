@@ -1,4 +1,5 @@
-"""Tensor parallelism on two GPUs.
+"""Tensor parallelism on 2, 4 and 8 GPUs (each world size skipped when fewer GPUs are
+visible).
 
 * The fused op (ms_tp_allreduce_rmsnorm_fp8) against the oracle and against
   the single-GPU kernel it replaces: the owned residual rows equal the
@@ -10,9 +11,9 @@
 * Exact activation scales: each rank quantises its K shard of a row with the
   all-reduced row amax, and its codes equal the single-GPU codes of that
   slice of the full row, bit for bit.
-* The model: fused-collective prefill logits against the same weights through
-  NCCL all-reduce + RMSNorm.
-Skipped when fewer than two GPUs are visible."""
+* The model: fused-collective prefill logits against the same weights through the
+  unfused path (an all-gather summed in rank order in fp32, then RMSNorm) bit for
+  bit, and against NCCL all-reduce + RMSNorm."""
 import os
 
 import pytest
@@ -33,6 +34,22 @@ def _case(seed, rows, world):
     residual = torch.randn(rows, H, generator=g).half()
     weight = (1 + 0.1 * torch.randn(H, generator=g)).half()
     return parts, residual, weight
+
+
+def _rank_order_sum(parts):
+    """The all-reduce the op computes: fp32, rank order, rounded to fp16 once."""
+    acc = torch.zeros_like(parts[0], dtype=torch.float32)
+    for p in parts:
+        acc = acc + p.float()
+    return acc.half()
+
+
+def _needs(world):
+    return pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < world,
+                              reason=f"needs {world} GPUs")
+
+
+WORLDS = [pytest.param(w, marks=_needs(w), id=f"tp{w}") for w in (2, 4, 8)]
 
 
 def _init_nccl(rank, world, port):
@@ -64,7 +81,7 @@ def _op_worker(rank, world, port, errq):
                 q, s = f.allreduce_norm_fp8(rows, res, weight.cuda(), 1e-6)
             torch.cuda.synchronize()
             # oracle: the all-reduce (fp32 sum in rank order -> fp16), the residual add, RMSNorm
-            total = torch.stack([p.float() for p in parts]).sum(0).half()
+            total = _rank_order_sum(parts)
             o_y, o_res = O.rmsnorm(total, weight, 1e-6, residual)
             o_q, o_s = O.quantize_rows(o_y)
             # the single-GPU kernel on the same summed rows
@@ -109,8 +126,7 @@ def _op_worker(rank, world, port, errq):
             else:
                 q, s = f.allreduce_norm_fp8(rows, res, nw, 1e-6, pushed=True)
             torch.cuda.synchronize()
-            parts = [kernels.fp8_gemm(*sh).float() for sh in shards]
-            total = torch.stack(parts).sum(0).half()
+            total = _rank_order_sum([kernels.fp8_gemm(*sh) for sh in shards])
             ky, kq, ks, kr = kernels.rmsnorm(total, nw, 1e-6, residual.cuda(), want_fp16=True, want_fp8=True)
             R = (rows + world - 1) // world
             own = slice(rank * R, min(rows, (rank + 1) * R))
@@ -121,7 +137,7 @@ def _op_worker(rank, world, port, errq):
                 assert torch.equal(s, ks) and torch.equal(q.view(torch.uint8), kq.view(torch.uint8)), \
                     f"pushed GEMM: codes / scales, case {it}"
             o_part = [O.fp8_gemm(*[t.cpu() for t in sh]).float() for sh in shards]
-            o_y, _ = O.rmsnorm(torch.stack(o_part).sum(0).half(), nw.cpu(), 1e-6, residual)
+            o_y, _ = O.rmsnorm(_rank_order_sum(o_part), nw.cpu(), 1e-6, residual)
             assert O.rel_l2(ky.cpu(), o_y) < 2e-3, f"pushed GEMM vs oracle, case {it}"
         assert _lib.device_status() == 0
 
@@ -143,8 +159,7 @@ def _op_worker(rank, world, port, errq):
             res = residual.cuda()
             out = f.rowpar_gemm_norm(*shards[rank], res, nw, 1e-6, want_fp16=want_h)
             torch.cuda.synchronize()
-            parts = [kernels.fp8_gemm(*sh).float() for sh in shards]
-            total = torch.stack(parts).sum(0).half()
+            total = _rank_order_sum([kernels.fp8_gemm(*sh) for sh in shards])
             ky, kq, ks, kr = kernels.rmsnorm(total, nw, 1e-6, residual.cuda(), want_fp16=True, want_fp8=True)
             R = (rows + world - 1) // world
             own = slice(rank * R, min(rows, (rank + 1) * R))
@@ -204,9 +219,9 @@ def _run(target, world, timeout):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_allreduce_rmsnorm_fp8_two_gpus():
-    _run(_op_worker, 2, 300)
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_allreduce_rmsnorm_fp8(world):
+    _run(_op_worker, world, 300)
 
 
 def _model_worker(rank, world, port, errq):
@@ -245,11 +260,17 @@ def _model_worker(rank, world, port, errq):
             finally:
                 reset_context()
         fused = prefill_logits()
-        runner.model.model.tp_fused = None  # the same weights through NCCL all-reduce + RMSNorm
+        runner.model.model.tp_fused = None  # the same weights, unfused
+        tp.set_ordered_sum(True)
+        ordered = prefill_logits()
+        tp.set_ordered_sum(False)
+        assert torch.equal(fused, ordered), "fused collective vs rank-order sum + RMSNorm: logits differ"
         nccl = prefill_logits()
         rel = ((fused - nccl).norm() / nccl.norm()).item()
         agree = (fused.argmax(-1) == nccl.argmax(-1)).float().mean().item()
-        assert rel < 5e-2 and agree > 0.85, (rel, agree)
+        if world == 2:  # two parts: NCCL's sum is the same sum
+            assert rel == 0.0, rel
+        assert rel < 0.5 and agree > 0.5, (rel, agree)
         assert _lib.device_status() == 0
         dist.barrier()
         dist.destroy_process_group()
@@ -260,13 +281,12 @@ def _model_worker(rank, world, port, errq):
     os._exit(0)
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp2_model_fused_collective_matches_nccl():
-    """Tensor-parallel Qwen3 prefill logits with the fused peer-memory op vs the
-    same weights through NCCL all-reduce + RMSNorm: the sums differ only in order
-    and rounding (fp32 in rank order vs NCCL's fp16 sum), which dynamic FP8
-    quantisation amplifies at the level of single codes (see the model-level bars
-    of test_model_gpu.py): logits agree to a relative L2 of 5e-2 with > 85 %
-    identical greedy tokens; a wrong row ownership or a missed peer row gives
-    relative errors of order 1."""
-    _run(_model_worker, 2, 400)
+@pytest.mark.parametrize("world", WORLDS)
+def test_model_fused_collective_matches_unfused(world):
+    """Tensor-parallel Qwen3 prefill logits with the fused peer-memory op vs the same
+    weights through the unfused path: identical bits when that path sums the ranks'
+    parts as the op does (all-gather, fp32 in rank order, one rounding). Against NCCL's
+    all-reduce the sums differ in order and rounding at more than two ranks, which the
+    dynamic FP8 quantisation between layers amplifies (one flipped code moves everything
+    after it): identical at two ranks, loosely bounded beyond."""
+    _run(_model_worker, world, 400)
