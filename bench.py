@@ -361,7 +361,10 @@ def kernel_rooflines(engine, batch, step_idx, hbm_peak):
     head_w = model.lm_head.weight
     hx = torch.randn(B, H, device=dev, generator=g).half()
     t = time_kernel(lambda: model.compute_logits(hx))
-    res["lm_head"] = dict(seconds=t, bytes=head_w.numel() * 2 + B * H * 2 + B * head_w.shape[0] * 2, per_layer=0)
+    # beside it, the library GEMM the reference calls (torch F.linear -> cuBLAS) on the same operands
+    t_lib = time_kernel(lambda: torch.nn.functional.linear(hx, head_w))
+    res["lm_head"] = dict(seconds=t, bytes=head_w.numel() * 2 + B * H * 2 + B * head_w.shape[0] * 2, per_layer=0,
+                          torch_linear_us=round(t_lib * 1e6, 2))
     tpf = runner.tp_fused
     world = tp.tp_size()
     if world > 1:

@@ -87,6 +87,15 @@ int ms_fp8_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* plan);
 int ms_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias, void* y,
                 int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
 
+/* fp16 GEMM on the same tcgen05 kernels (kind::f16): y [M, N] fp16 = fp16(x [M, K] .
+ * w [N, K]^T), fp32 accumulation, both operands K-contiguous and 16-byte aligned,
+ * K % 8 == 0. Replaces the LM head's F.linear (microserve/layers/embed_head.py:35-36,
+ * ParallelLMHead.forward; the vocab-parallel slice of it under tensor parallelism).
+ * workspace: at least ms_f16_gemm_workspace_size(M, N, K) bytes (may be 0). */
+size_t ms_f16_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+int ms_f16_gemm(const void* x, const void* w, void* y, int64_t M, int64_t N, int64_t K, void* workspace,
+                size_t workspace_bytes, void* stream);
+
 /* RMSNorm over rows of H (H % 16 == 0, H <= 32768), optionally fused with the residual
  * add and an FP8 quantisation of the output:
  *   residual == NULL: y = fp16(fp16(x * rsqrt(mean(x^2) + eps)) * weight)

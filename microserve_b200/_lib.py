@@ -42,6 +42,8 @@ SIGNATURES: dict[str, tuple] = {
     "ms_quantize_rows_fp8": (i32, [vp, i64, i64, i64, vp, vp, vp]),
     "ms_fp8_gemm_workspace_size": (sz, [i64, i64, i64]),
     "ms_fp8_gemm_plan": (i32, [i64, i64, i64, i32, C.POINTER(C.c_int)]),
+    "ms_f16_gemm_workspace_size": (C.c_size_t, [i64, i64, i64]),
+    "ms_f16_gemm": (i32, [vp, vp, vp, i64, i64, i64, vp, C.c_size_t, vp]),
     "ms_fp8_gemm": (i32, [vp, vp, vp, vp, vp, vp, i64, i64, i64, vp, sz, vp]),
     "ms_rmsnorm": (i32, [vp, vp, vp, i64, i64, f32, vp, vp, vp, vp, vp]),
     "ms_silu_mul": (i32, [vp, i64, i64, vp, vp, vp, vp]),

@@ -107,6 +107,29 @@ int ms_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw
                     "ms_fp8_gemm");
 }
 
+size_t ms_f16_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || K > INT32_MAX / 2) return 0;
+  return ms::gemm_workspace_bytes((int)M, (int)N, (int)(2 * K), num_sms());
+}
+
+int ms_f16_gemm(const void* x, const void* w, void* y, int64_t M, int64_t N, int64_t K, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX / 2)
+    return fail(MS_ERR_INVALID, "ms_f16_gemm: bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N,
+                (long long)K);
+  if (M == 0 || N == 0) return MS_OK;
+  if (!x || !w || !y) return fail(MS_ERR_INVALID, "ms_f16_gemm: null pointer");
+  if (K % 8 != 0) return fail(MS_ERR_UNSUPPORTED, "ms_f16_gemm: K=%lld is not a multiple of 8", (long long)K);
+  if (((uintptr_t)x & 15) != 0 || ((uintptr_t)w & 15) != 0)
+    return fail(MS_ERR_INVALID, "ms_f16_gemm: x and w must be 16-byte aligned");
+  const size_t need = ms::gemm_workspace_bytes((int)M, (int)N, (int)(2 * K), num_sms());
+  if (workspace_bytes < need || (need > 0 && workspace == nullptr))
+    return fail(MS_ERR_WORKSPACE, "ms_f16_gemm: workspace %zu < %zu bytes", workspace_bytes, need);
+  return check_cuda(ms::launch_fp8_gemm(x, nullptr, w, nullptr, nullptr, y, (int)M, (int)N, (int)(2 * K), workspace,
+                                        workspace_bytes, num_sms(), S(stream), nullptr, nullptr, true),
+                    "ms_f16_gemm");
+}
+
 int ms_rmsnorm(const void* x, const void* residual, const void* weight, int64_t M, int64_t H, float eps,
                void* residual_out, void* y, void* yq, float* sy, void* stream) {
   if (M < 0 || H <= 0) return fail(MS_ERR_INVALID, "ms_rmsnorm: bad sizes");

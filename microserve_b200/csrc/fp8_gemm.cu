@@ -58,6 +58,7 @@ struct GemmArgs {
   float* ws;   // [G][BN][kBM] fp32 partial tiles (stream-K fixup)
   int* flags;  // [G] partial-ready flags; zero before and after every launch
   int tma_y;   // 1: the output tensor map is valid (N % 8 == 0, y 16-byte aligned)
+  int f16;     // 1: fp16 operands (kind::f16; K counted in bytes, sx / sw null = 1)
   // Row-parallel push (tensor parallelism, rp_R > 0): instead of y, output row m
   // goes to rank m / rp_R's receive slot [b][rp_rank][m mod rp_R] (b = the parity
   // of the epoch word *rp_ctrl), over NVLink for the other ranks (tp_rows.cuh).
@@ -225,6 +226,17 @@ __device__ __forceinline__ void load_stage(const CUtensorMap* map, uint32_t dst,
   } else {
     tma_load_3d(map, dst, bar, 0, row, k * CH);
   }
+}
+
+// fp16 operands: the same 32 bytes of K per instruction (16 elements), and the
+// same instruction descriptor (format code 0 is f16 for kind::f16, e4m3 for
+// kind::f8f6f4).
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accum));
 }
 
 __device__ __forceinline__ void umma_f8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accum) {
@@ -421,7 +433,7 @@ __device__ __forceinline__ void split_epilogue(const GemmArgs& args, uint32_t ac
 // warps 2-5 are the epilogue (TMEM lane quarter = warp % 4). The other lanes
 // of warps 0-1 wait at __syncwarp so every warp reaches the final block
 // barrier converged (a partially arrived warp would count as arrived).
-template <int BN, int CH>
+template <int BN, int CH, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ GemmArgs args) {
@@ -530,13 +542,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t a_addr = smem_u32(smem + s * C::kStageBytes);
           const uint32_t b_addr = a_addr + C::kABytes;
+          // The start-address field of a descriptor is (address >> 4) in 14 bits and
+          // shared addresses stay below 2^18, so stepping through the stage is a
+          // constant add to the stage's first descriptor: the single issuing thread
+          // keeps up with the tensor core on small token tiles.
+          const uint64_t da0 = smem_desc_sw128(a_addr), db0 = smem_desc_sw128(b_addr);
 #pragma unroll
           for (int c = 0; c < CH; ++c) {
 #pragma unroll
             for (int kk = 0; kk < kChunk / 32; ++kk) {
-              umma_f8(acc, smem_desc_sw128(a_addr + c * C::kChunkA + kk * 32),
-                      smem_desc_sw128(b_addr + c * C::kChunkB + kk * 32), C::kIdesc,
-                      (j > 0 || c > 0 || kk > 0) ? 1u : 0u);
+              const uint64_t da = da0 + (uint64_t)((c * C::kChunkA + kk * 32) >> 4);
+              const uint64_t db = db0 + (uint64_t)((c * C::kChunkB + kk * 32) >> 4);
+              const uint32_t accum = (j > 0 || c > 0 || kk > 0) ? 1u : 0u;
+              if constexpr (F16)
+                umma_f16(acc, da, db, C::kIdesc, accum);
+              else
+                umma_f8(acc, da, db, C::kIdesc, accum);
             }
           }
           umma_commit(&empty[s]);
@@ -573,10 +594,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (owner || args.splits > 0) {
         // scales are inputs: fetch them while the tile is still accumulating
         for (int j = et; j < cols; j += 128) {
-          s_sx[b * BN + j] = args.sx[m0 + j];
+          s_sx[b * BN + j] = args.sx != nullptr ? args.sx[m0 + j] : 1.f;
           if (args.rp_R > 0) s_rows[b * BN + j] = rp_row(args, m0 + j, rp_b);
         }
-        swn = n_ok ? args.sw[n] : 0.f;
+        swn = n_ok ? (args.sw != nullptr ? args.sw[n] : 1.f) : 0.f;
         bn = (n_ok && args.bias != nullptr) ? __half2float(args.bias[n]) : 0.f;
       }
       if (!mbar_wait(&acc_full[b], ((uint32_t)seg >> 1) & 1u)) break;
@@ -708,6 +729,7 @@ constexpr uint32_t kWideIdesc = (1u << 4) | ((uint32_t)(kWideBN >> 3) << 17) | (
 static_assert(kWideSmem <= 227 * 1024, "shared memory budget");
 static_assert(2 * kWideBN * kBM * 2 <= kWideStages * kWideStageBytes, "staged output tile fits the stages");
 
+template <bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                          const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ GemmArgs args) {
@@ -786,12 +808,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t a_addr = smem_u32(smem + s * kWideStageBytes);
           const uint32_t b_addr = a_addr + kWideABytes;
+          const uint64_t da0 = smem_desc_sw128(a_addr), db0 = smem_desc_sw128(b_addr);  // see fp8_gemm_kernel
 #pragma unroll
           for (int kk = 0; kk < kChunk / 32; ++kk) {
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
-              umma_f8(tmem + (uint32_t)(mt * kWideBN), smem_desc_sw128(a_addr + mt * kBM * kChunk + kk * 32),
-                      smem_desc_sw128(b_addr + kk * 32), kWideIdesc, (k > 0 || kk > 0) ? 1u : 0u);
+              const uint64_t da = da0 + (uint64_t)((mt * kBM * kChunk + kk * 32) >> 4);
+              const uint64_t db = db0 + (uint64_t)((kk * 32) >> 4);
+              const uint32_t accum = (k > 0 || kk > 0) ? 1u : 0u;
+              if constexpr (F16)
+                umma_f16(tmem + (uint32_t)(mt * kWideBN), da, db, kWideIdesc, accum);
+              else
+                umma_f8(tmem + (uint32_t)(mt * kWideBN), da, db, kWideIdesc, accum);
             }
           }
           umma_commit(&empty[s]);
@@ -813,12 +841,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = (int)(t % args.tiles_m) * kWideBN;
       const int cols = min(kWideBN, args.M - m0);
       epi_sync();  // the previous tile's readers of s_sx are done
-      for (int j = et; j < cols; j += 128) s_sx[j] = args.sx[m0 + j];
+      for (int j = et; j < cols; j += 128) s_sx[j] = args.sx != nullptr ? args.sx[m0 + j] : 1.f;
       float swn[2], bn[2];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
         const int n = n0 + mt * kBM + row;
-        swn[mt] = n < N ? args.sw[n] : 0.f;
+        swn[mt] = n < N ? (args.sw != nullptr ? args.sw[n] : 1.f) : 0.f;
         bn[mt] = (n < N && args.bias != nullptr) ? __half2float(args.bias[n]) : 0.f;
       }
       if (!mbar_wait(acc_full, (uint32_t)tile & 1u)) break;
@@ -969,13 +997,13 @@ bool make_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int
   return true;
 }
 
-template <int BN, int CH>
-cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs& args,
-                      cudaStream_t stream) {
+template <int BN, int CH, bool F16>
+cudaError_t launch_tc_kind(const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs& args,
+                           cudaStream_t stream) {
   using C = Cfg<BN, CH>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<BN, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<BN, CH, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set = true;
@@ -984,8 +1012,15 @@ cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const CUtens
   // (one per SM) must become resident. The preceding grid never waits on this
   // one, so its SMs free up; the next grid cannot start before every CTA here
   // has triggered (after issuing its last load), i.e. before all are resident.
-  return launch_kernel(fp8_gemm_kernel<BN, CH>, dim3(args.G), dim3(kThreads), C::kSmemBytes, stream, mw, mx, my,
-                       args);
+  return launch_kernel(fp8_gemm_kernel<BN, CH, F16>, dim3(args.G), dim3(kThreads), C::kSmemBytes, stream, mw, mx,
+                       my, args);
+}
+
+template <int BN, int CH>
+cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& my, const GemmArgs& args,
+                      cudaStream_t stream) {
+  return args.f16 ? launch_tc_kind<BN, CH, true>(mw, mx, my, args, stream)
+                  : launch_tc_kind<BN, CH, false>(mw, mx, my, args, stream);
 }
 
 template <int BN>
@@ -1124,8 +1159,9 @@ size_t gemm_workspace_bytes(int M, int N, int K, int num_sms) {
 
 cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,
                             void* y, int M, int N, int K, void* workspace, size_t workspace_bytes, int num_sms,
-                            cudaStream_t stream, const TpRows* rp, bool* tail) {
+                            cudaStream_t stream, const TpRows* rp, bool* tail, bool f16) {
   if (M == 0 || N == 0) return cudaSuccess;
+  if (f16 && (K % 16 != 0 || rp != nullptr)) return cudaErrorInvalidValue;
   if (rp != nullptr && (K % 16 != 0 || rp->H != N || rp->M != M)) return cudaErrorInvalidValue;
   if (K % 16 != 0) {
     dim3 grid((N + 127) / 128, M);
@@ -1155,14 +1191,23 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
     args.G = p.ctas;
     args.dp = 1;
     args.tma_y = tma_y ? 1 : 0;
+    args.f16 = f16 ? 1 : 0;
     args.sx = sx;
     args.sw = sw;
     args.bias = (const __half*)bias;
     args.y = (__half*)y;
+    if (f16) {
+      static const cudaError_t attr =
+          cudaFuncSetAttribute(fp8_gemm_wide_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmem);
+      if (attr != cudaSuccess) return attr;
+      return launch_kernel(fp8_gemm_wide_kernel<true>, dim3(args.G), dim3(kThreads), kWideSmem, stream, mw, mx, my,
+                           args);
+    }
     static const cudaError_t attr =
-        cudaFuncSetAttribute(fp8_gemm_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmem);
+        cudaFuncSetAttribute(fp8_gemm_wide_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmem);
     if (attr != cudaSuccess) return attr;
-    return launch_kernel(fp8_gemm_wide_kernel, dim3(args.G), dim3(kThreads), kWideSmem, stream, mw, mx, my, args);
+    return launch_kernel(fp8_gemm_wide_kernel<false>, dim3(args.G), dim3(kThreads), kWideSmem, stream, mw, mx, my,
+                         args);
   }
   if (!make_map(&mw, wq, N, K, kBM, p.ch) || !make_map(&mx, xq, M, K, bn, p.ch)) return cudaErrorInvalidValue;
   GemmArgs args = {};
@@ -1199,6 +1244,7 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   args.dp = p.dp;
   args.splits = p.splits;
   args.tma_y = tma_y ? 1 : 0;
+  args.f16 = f16 ? 1 : 0;
   if (p.splits > args.KT) return cudaErrorInvalidValue;  // a K part without steps
   args.sx = sx;
   args.sw = sw;

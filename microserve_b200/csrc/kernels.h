@@ -67,8 +67,10 @@ struct TpRows;
 // rp): in, a request to do the tensor-parallel row work (reduce + residual +
 // RMSNorm + FP8 + gather, the fields of *rp) in the GEMM's own tail; out, whether
 // it will (otherwise the caller launches the separate op with pushed rows).
+// f16: fp16 operands x [M, K/2] and w [N, K/2] (K in bytes, a multiple of 16), no
+// scales (sx, sw null), no row-parallel push: y = fp16(x . w^T), fp32 accumulation.
 cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,
                             void* y, int M, int N, int K, void* workspace, size_t workspace_bytes, int num_sms,
-                            cudaStream_t stream, const TpRows* rp = nullptr, bool* tail = nullptr);
+                            cudaStream_t stream, const TpRows* rp = nullptr, bool* tail = nullptr, bool f16 = false);
 
 }  // namespace ms

@@ -125,6 +125,24 @@ def fp8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Ten
     return y
 
 
+def f16_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y [M, N] fp16 = x [M, K] . w [N, K]^T with fp32 accumulation (the LM head's
+    F.linear) on this library's tcgen05 GEMM."""
+    _cuda(x, "x")
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K or x.dtype != torch.float16 or w.dtype != torch.float16:
+        raise ValueError("f16_gemm: expected fp16 x [M, K] and w [N, K]")
+    if not (x.is_contiguous() and w.is_contiguous()):
+        raise ValueError("f16_gemm: operands must be contiguous")
+    y = out if out is not None else torch.empty((M, N), dtype=torch.float16, device=x.device)
+    lib = _lib.load()
+    ws = workspace.get(lib.ms_f16_gemm_workspace_size(M, N, K), x.device, "gemm")
+    check(lib.ms_f16_gemm(ptr(x), ptr(w), ptr(y), M, N, K, ptr(ws), 0 if ws is None else ws.numel(), stream_ptr()),
+          "ms_f16_gemm")
+    return y
+
+
 def fp8_gemm_rowpar(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor, bases, rank: int,
                     world: int, max_rows: int) -> None:
     """Row-parallel FP8 GEMM whose output rows go to their owners' receive slots in

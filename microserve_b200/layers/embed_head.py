@@ -1,7 +1,7 @@
 """Token embedding and LM head (microserve/layers/embed_head.py:5-36).
 
-Single GPU: plain fp16 embedding lookup and LM-head projection, as in the
-reference. Under tensor parallelism both are vocab-parallel: each rank holds
+Single GPU: plain fp16 embedding lookup and LM-head projection (fp16 operands,
+fp32 accumulation, on this library's tcgen05 GEMM), as in the reference. Under tensor parallelism both are vocab-parallel: each rank holds
 vocab rows [r*V/t, (r+1)*V/t); the embedding sums the masked lookups over the
 group, and the head returns this rank's logits slice (the runner's greedy
 sampler reduces (max, index) pairs across ranks instead of gathering logits).
@@ -44,5 +44,10 @@ class ParallelLMHead(VocabParallelEmbedding):
         super().__init__(num_embeddings, embedding_dim)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """Logits of this rank's vocab slice (the full vocab when tp_size == 1)."""
+        """Logits of this rank's vocab slice (the full vocab when tp_size == 1): the
+        library's fp16 tcgen05 GEMM on the GPU (host tensors: the CPU tests of the
+        tensor-parallel logic)."""
+        if x.is_cuda:
+            from microserve_b200 import kernels
+            return kernels.f16_gemm(x.contiguous(), self.weight)
         return F.linear(x, self.weight)

@@ -134,6 +134,35 @@ def test_fp8_gemm_sequence_no_stale_state():
         assert (y.float() - ref.float()).abs().max().item() <= tol, (M, N, K)
 
 
+F16_GEMM_SHAPES = [
+    # the LM head at 256 sequences: the full Qwen3 vocabulary, and its vocab-parallel shard at TP = 8
+    (256, 151936, 4096), (256, 18992, 4096),
+    # one and a few rows (decode of small batches), split-K shards, a prefill-sized M (stream-K / whole tiles)
+    (1, 18992, 4096), (7, 1000, 64), (64, 24576, 1024), (256, 768, 4096), (300, 2048, 1024), (1024, 4096, 4096),
+    # 256-row x 256-token tiles with a ragged last tile; N % 8 != 0 (no bulk store); K % 64 != 0
+    (200, 19000, 512), (37, 1001, 520), (129, 24576, 272),
+]
+
+
+@pytest.mark.parametrize("M,N,K", F16_GEMM_SHAPES)
+def test_f16_gemm_vs_fp32(M, N, K):
+    """The LM head's fp16 GEMM (ms_f16_gemm, kind::f16 on the tcgen05 kernels) against an
+    fp32 product of the same fp16 operands, and against torch's F.linear (the reference's
+    call, microserve/layers/embed_head.py:35-36)."""
+    from microserve_b200 import kernels
+    g = torch.Generator(device=DEV).manual_seed(M * 3 + N + K)
+    x = torch.randn(M, K, generator=g, device=DEV).half()
+    w = (torch.randn(N, K, generator=g, device=DEV) * 0.02).half()
+    y = kernels.f16_gemm(x, w)
+    ref = x.float() @ w.float().t()
+    # exact products, fp32 sums in another order, one rounding to fp16: within 2 fp16 ulps
+    tol = 2e-3 * max(1.0, ref.abs().max().item())
+    assert (y.float() - ref).abs().max().item() <= tol
+    lin = torch.nn.functional.linear(x, w)
+    assert (y.float() - lin.float()).abs().max().item() <= tol
+    assert (y.float() - ref).norm().item() <= 1e-3 * ref.norm().item()
+
+
 @pytest.mark.parametrize("M,N,K", [(5, 384, 256), (200, 19000, 256), (200, 19000, 512)])
 def test_fp8_gemm_bias(M, N, K):
     from microserve_b200 import kernels
