@@ -81,7 +81,8 @@ size_t ms_fp8_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
  * (0 = the CUDA-core kernel for K % 16 != 0), plan[1] CTAs, plan[2] K parts
  * per weight tile (split-K; 0 otherwise), plan[3] 1 for 256-row x 256-token
  * tiles, plan[4] 1 for whole tiles (0: split-K or stream-K), plan[5] 128-byte
- * K chunks per pipeline stage. No reference counterpart (the reference's
+ * K chunks per pipeline stage, plan[6] 1 for 256 x 256 tiles on pairs of SMs
+ * (tcgen05 cta_group::2; plan must hold 7 ints). No reference counterpart (the reference's
  * `_fp8_mm` grid is fixed, microserve/layers/fp8_linear.py:75-77). */
 int ms_fp8_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* plan);
 int ms_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias, void* y,

@@ -711,6 +711,253 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Arrive (release, cluster scope) on a barrier given by its shared::cluster address.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Every thread of every CTA of the cluster.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// 2-SM tiles (tcgen05 cta_group::2) for prefill-sized M: a cluster of two CTAs
+// computes a 256 weight-row x 256 token output tile with ONE MMA per K step of
+// 32 bytes. Each CTA loads half of each operand into its own shared memory (128
+// weight rows, 128 tokens: a stage is 2 x 32 KB per CTA instead of 96 KB for a
+// 128 x 256 tile on one SM), the leader CTA (cluster rank 0) issues the MMAs,
+// which read both CTAs' halves, and each CTA's TMEM receives its 128 weight rows
+// x 256 tokens. So every output needs half the L2 -> SM bytes of the one-SM
+// tile (per-SM ingest bounds the one-SM kernel). No multicast: each CTA's TMA
+// loads bring only its own half, from this GPU's memory; their completion is
+// counted on the leader's barrier (.cta_group::2). Tiles are dealt whole to the
+// pairs, with double-buffered accumulators as in fp8_gemm_kernel.
+//   full[s]     leader only: both CTAs' loads of stage s landed (armed by the leader
+//               with both halves' bytes)
+//   empty[s]    each CTA: the MMAs reading stage s are done (one commit, multicast
+//               to both CTAs)
+//   acc_full[b] each CTA: accumulator b complete (multicast commit)
+//   acc_empty[b] leader: both CTAs' epilogues have drained accumulator b
+//               (128 local + 128 remote arrivals)
+constexpr int kPairBN = 256;                          // tokens per tile (128 per CTA)
+constexpr int kPairRows = 2 * kBM;                    // weight rows per tile (128 per CTA)
+constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;        // shared address of the same object in rank 0
+template <int CH>
+struct PairCfg {
+  static constexpr int kABytes = CH * kBM * kChunk;                // this CTA's weight rows
+  static constexpr int kStageBytes = kABytes + CH * (kPairBN / 2) * kChunk;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSxBytes = 2 * kPairBN * 4;
+  static constexpr int kFit = (227 * 1024 - 1024 - kBarBytes - kSxBytes) / kStageBytes;
+  static constexpr int kStages = kFit > 6 ? 6 : kFit;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarBytes + kSxBytes;
+  // D=f32, A=B=e4m3 (or f16 for kind::f16), K-major, N=256, M=256
+  static constexpr uint32_t kIdesc =
+      (1u << 4) | ((uint32_t)(kPairBN >> 3) << 17) | ((uint32_t)(kPairRows >> 4) << 24);
+  static_assert(kStages >= 2, "shared memory budget");
+};
+
+__device__ __forceinline__ void tma_load_pair_2d(const CUtensorMap* map, uint32_t dst, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_pair_3d(const CUtensorMap* map, uint32_t dst, uint32_t bar, int c0, int c1,
+                                                 int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4}], [%5];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+template <int CH>
+__device__ __forceinline__ void load_pair_stage(const CUtensorMap* map, uint32_t dst, uint32_t bar, int k, int row) {
+  if constexpr (CH == 1) {
+    tma_load_pair_2d(map, dst, bar, k * kChunk, row);
+  } else {
+    tma_load_pair_3d(map, dst, bar, 0, row, k * CH);
+  }
+}
+template <bool F16>
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accum) {
+  if constexpr (F16) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(accum));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(accum));
+  }
+}
+// Completion of this thread's earlier MMAs arrives on the barrier at the same
+// shared offset in both CTAs of the pair.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((unsigned short)3)
+      : "memory");
+}
+
+template <int CH, bool F16>
+__global__ void __launch_bounds__(kThreads, 1)
+    fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                         const __grid_constant__ GemmArgs args) {
+  using C = PairCfg<CH>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];  // aligned by hand, see fp8_gemm_kernel
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* s_sx = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes + C::kBarBytes);  // [2][256]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = (int)cluster_ctarank();
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int KT = args.KT;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * 128);
+    }
+    fence_barrier_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_x) : "memory");
+  }
+  if (warp == 1) {  // the same warp in both CTAs allocates the pair's accumulators
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  cluster_sync_all();  // both CTAs' barriers exist before either signals the other
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer (both CTAs: this CTA's halves)
+      int i = 0;
+      bool ok = true, waited = false;
+      for (int64_t t = pair; ok && t < args.T; t += pairs) {
+        const int n0 = (int)(t / args.tiles_m) * kPairRows + rank * kBM;
+        const int m0 = (int)(t % args.tiles_m) * kPairBN + rank * (kPairBN / 2);
+        for (int k = 0; k < KT; ++k, ++i) {
+          const int s = i % C::kStages;
+          if (!mbar_wait(&empty[s], ((uint32_t)(i / C::kStages) & 1u) ^ 1u)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::kStageBytes);
+          const uint32_t bar = smem_u32(&full[s]) & kPeerBitMask;  // the leader's full[s]
+          const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
+          load_pair_stage<CH>(&tmap_w, sa, bar, k, n0);
+          if (!waited) {
+            pdl_wait();
+            waited = true;
+          }
+          load_pair_stage<CH>(&tmap_x, sa + C::kABytes, bar, k, m0);
+        }
+      }
+      pdl_trigger();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {  // MMA issuer: the leader only
+      int i = 0, tile = 0;
+      for (int64_t t = pair; t < args.T; t += pairs, ++tile) {
+        const int b = tile & 1;
+        if (!mbar_wait(&acc_empty[b], (((uint32_t)tile >> 1) & 1u) ^ 1u)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc = tmem + (uint32_t)(b * kPairBN);
+        bool ok = true;
+        for (int k = 0; k < KT; ++k, ++i) {
+          const int s = i % C::kStages;
+          if (!mbar_wait(&full[s], (uint32_t)(i / C::kStages) & 1u)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = smem_u32(smem + s * C::kStageBytes);
+          const uint64_t da0 = smem_desc_sw128(a_addr), db0 = smem_desc_sw128(a_addr + C::kABytes);
+#pragma unroll
+          for (int c = 0; c < CH; ++c) {
+#pragma unroll
+            for (int kk = 0; kk < kChunk / 32; ++kk) {
+              const uint64_t da = da0 + (uint64_t)((c * kBM * kChunk + kk * 32) >> 4);
+              const uint64_t db = db0 + (uint64_t)((c * (kPairBN / 2) * kChunk + kk * 32) >> 4);
+              umma_pair<F16>(acc, da, db, C::kIdesc, (k > 0 || c > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit_pair(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[b]);
+      }
+    }
+    __syncwarp();
+  } else {  // epilogue: warps 2..5 -> TMEM lane quarters 2, 3, 0, 1 of this CTA's 128 rows
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int et = threadIdx.x - 64;
+    const uint32_t leader_acc_empty = smem_u32(acc_empty) & kPeerBitMask;
+    pdl_wait();
+    int tile = 0;
+    for (int64_t t = pair; t < args.T; t += pairs, ++tile) {
+      const int b = tile & 1;
+      const int n = (int)(t / args.tiles_m) * kPairRows + rank * kBM + row;
+      const int m0 = (int)(t % args.tiles_m) * kPairBN;
+      const int cols = min(kPairBN, args.M - m0);
+      for (int j = et; j < cols; j += 128) s_sx[b * kPairBN + j] = args.sx != nullptr ? args.sx[m0 + j] : 1.f;
+      const bool n_ok = n < args.N;
+      const float swn = n_ok ? (args.sw != nullptr ? args.sw[n] : 1.f) : 0.f;
+      const float bn = (n_ok && args.bias != nullptr) ? __half2float(args.bias[n]) : 0.f;
+      if (!mbar_wait(&acc_full[b], ((uint32_t)tile >> 1) & 1u)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      epi_sync();  // s_sx filled
+      const uint32_t acc = tmem + (uint32_t)(b * kPairBN) + ((uint32_t)(q * 32) << 16);
+      for (int c0 = 0; c0 < cols; c0 += 16) {
+        float v[16];
+        tmem_ld16(acc + (uint32_t)c0, v);
+        out16(args, v, s_sx + b * kPairBN, swn, bn, m0, c0, cols, n, nullptr, row);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      epi_sync();  // every thread has read s_sx[b] and accumulator b
+      mbar_arrive_remote(leader_acc_empty + (uint32_t)(b * 8));
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  // nothing of either CTA is touched by the other after this point
+  cluster_sync_all();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+  cluster_sync_all();  // both CTAs have released the pair's accumulators before either exits
+}
+
 // Wide tiles for decode batches of 129..256 tokens with many weight tiles (the
 // gate/up projection): 256 weight rows x 256 tokens per tile, computed as two
 // M = 128 MMAs that share every activation stage. The activations are read once
@@ -1023,6 +1270,35 @@ cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const CUtens
                   : launch_tc_kind<BN, CH, false>(mw, mx, my, args, stream);
 }
 
+template <int CH, bool F16>
+cudaError_t launch_pair_kind(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& args, cudaStream_t stream) {
+  using C = PairCfg<CH>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_pair_kernel<CH, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  if (args.G % 2 != 0) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(args.G);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;  // the two CTAs of a tile: one pair of SMs
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl_enabled.load(std::memory_order_relaxed) ? 2 : 1;
+  MS_COUNT_LAUNCH();
+  return cudaLaunchKernelEx(&cfg, fp8_gemm_pair_kernel<CH, F16>, mw, mx, args);
+}
+
 template <int BN>
 cudaError_t launch_bn(int ch, const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& my,
                       const GemmArgs& args, cudaStream_t stream) {
@@ -1033,7 +1309,7 @@ constexpr size_t kFlagBytes = 1024;  // per-CTA partial-ready flags at the start
 constexpr int kMinUnitsPerCta = 4;
 
 struct Plan {
-  int bn, ch, ctas, dp, splits, wide;
+  int bn, ch, ctas, dp, splits, wide, pair;
 };
 
 // Tile shape and scheduling for an M x N x K problem (rules fitted to B200
@@ -1057,8 +1333,8 @@ struct Plan {
 // loop and keep direct stores).
 //  * M > 256 (prefill): 256-token tiles; whole tiles when they fill the SMs
 //    evenly, else stream-K over tiles x K-steps.
-Plan make_plan(int M, int N, int K, int num_sms) {
-  Plan p{256, (K % kChunk == 0) ? 2 : 1, 1, 0, 0, 0};
+Plan make_plan(int M, int N, int K, int num_sms, bool allow_pair = true) {
+  Plan p{256, (K % kChunk == 0) ? 2 : 1, 1, 0, 0, 0, 0};
   const int64_t tiles_n = (N + kBM - 1) / kBM;
   if (M > 128 && M <= 256 && tiles_n > num_sms) {  // e.g. gate/up: 256-row x 256-token tiles
     const int64_t T = (N + kWideRows - 1) / kWideRows;
@@ -1095,6 +1371,21 @@ Plan make_plan(int M, int N, int K, int num_sms) {
       int64_t sp = s < steps ? s : steps;
       p.splits = (int)(sp < 8 ? sp : 8);
       p.ctas = (int)(tiles_n * p.splits);
+      return p;
+    }
+  }
+  if (M > 256 && allow_pair && K <= 8192) {
+    // prefill: 256 x 256 tiles on SM pairs (fp8_gemm_pair_kernel) when they fill the
+    // pairs evenly (B200, 8192 tokens: q/k/v 192.9 vs 223.3 us for one-SM tiles, o and
+    // gate/up within 1 %, the 12288-long K of down 417 vs 395 us, so not for long K)
+    const int64_t pairs = num_sms / 2;
+    const int64_t T2 = ((N + kPairRows - 1) / kPairRows) * ((M + kPairBN - 1) / kPairBN);
+    const int64_t waves2 = (T2 + pairs - 1) / pairs;
+    if (pairs >= 1 && T2 >= pairs && (double)T2 / ((double)waves2 * pairs) >= 0.9) {
+      p.pair = 1;
+      p.dp = 1;
+      p.bn = kPairBN;
+      p.ctas = (int)(2 * pairs);
       return p;
     }
   }
@@ -1138,7 +1429,7 @@ void gemm_plan(int M, int N, int K, int num_sms, int* out) {
   if (K % 16 != 0) {  // CUDA-core kernel: one thread per output, 128-column blocks
     out[0] = 0;
     out[1] = (int)((N + 127) / 128) * M;
-    out[2] = out[3] = out[5] = 0;
+    out[2] = out[3] = out[5] = out[6] = 0;
     out[4] = 1;
     return;
   }
@@ -1149,12 +1440,19 @@ void gemm_plan(int M, int N, int K, int num_sms, int* out) {
   out[3] = p.wide;
   out[4] = p.dp;
   out[5] = p.ch;
+  out[6] = p.pair;
 }
 
 size_t gemm_workspace_bytes(int M, int N, int K, int num_sms) {
   if (K % 16 != 0 || M <= 0) return 0;
-  const Plan p = make_plan(M, N, K, num_sms);
-  return p.dp ? 0 : kFlagBytes + (size_t)p.ctas * p.bn * kBM * sizeof(float);
+  // the plan of a plain call, and of a row-parallel call (no SM pairs) of the same shape
+  size_t need = 0;
+  for (int allow_pair = 0; allow_pair < 2; ++allow_pair) {
+    const Plan p = make_plan(M, N, K, num_sms, allow_pair != 0);
+    const size_t b = p.dp ? 0 : kFlagBytes + (size_t)p.ctas * p.bn * kBM * sizeof(float);
+    need = b > need ? b : need;
+  }
+  return need;
 }
 
 cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, const float* sw, const void* bias,
@@ -1168,7 +1466,8 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
     return launch_kernel(fp8_gemm_simt_kernel, grid, dim3(128), 0, stream, (const uint8_t*)xq, (const uint8_t*)wq, M,
                          N, K, sx, sw, (const __half*)bias, (__half*)y);
   }
-  const Plan p = make_plan(M, N, K, num_sms);
+  // (row-parallel push and the tensor-parallel tail are written for one-SM tiles)
+  const Plan p = make_plan(M, N, K, num_sms, rp == nullptr);
   const int bn = p.bn;
   if (!p.dp && (gemm_workspace_bytes(M, N, K, num_sms) > workspace_bytes || workspace == nullptr))
     return cudaErrorInvalidValue;
@@ -1177,6 +1476,27 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   // (and a local y: pushed rows leave through plain stores).
   const bool tma_y = rp == nullptr && N % 8 == 0 && ((uintptr_t)y & 15) == 0 && make_map(&my, y, M, N, bn, 0);
   if (!tma_y) memset(&my, 0, sizeof(my));
+  if (p.pair) {
+    if (!make_map(&mw, wq, N, K, kBM, p.ch) || !make_map(&mx, xq, M, K, kPairBN / 2, p.ch))
+      return cudaErrorInvalidValue;
+    GemmArgs args = {};
+    args.M = M;
+    args.N = N;
+    args.K = K;
+    args.KT = (K + kChunk * p.ch - 1) / (kChunk * p.ch);
+    args.tiles_m = (M + kPairBN - 1) / kPairBN;
+    args.T = (int64_t)((N + kPairRows - 1) / kPairRows) * args.tiles_m;
+    args.G = p.ctas;
+    args.dp = 1;
+    args.sx = sx;
+    args.sw = sw;
+    args.bias = (const __half*)bias;
+    args.y = (__half*)y;
+    args.f16 = f16 ? 1 : 0;
+    if (p.ch == 2)
+      return f16 ? launch_pair_kind<2, true>(mw, mx, args, stream) : launch_pair_kind<2, false>(mw, mx, args, stream);
+    return f16 ? launch_pair_kind<1, true>(mw, mx, args, stream) : launch_pair_kind<1, false>(mw, mx, args, stream);
+  }
   if (p.wide) {
     if (rp != nullptr) return cudaErrorInvalidValue;  // row-parallel outputs are never that wide
     if (!make_map(&mw, wq, N, K, kWideRows, 1) || !make_map(&mx, xq, M, K, kWideBN, 1)) return cudaErrorInvalidValue;

@@ -134,11 +134,43 @@ def test_fp8_gemm_sequence_no_stale_state():
         assert (y.float() - ref.float()).abs().max().item() <= tol, (M, N, K)
 
 
+PAIR_GEMM_SHAPES = [
+    # prefill-sized tiles on SM pairs (tcgen05 cta_group::2, 256 x 256 per pair): 2-chunk stages; ragged M,
+    # N and K % 128 != 0 (1-chunk stages); 96 weight tiles; one K step per tile
+    (8192, 4096, 4096), (8000, 4000, 1040), (2048, 24576, 1024), (4096, 9472, 256),
+]
+
+
+@pytest.mark.parametrize("M,N,K", PAIR_GEMM_SHAPES)
+def test_fp8_gemm_on_sm_pairs(M, N, K):
+    """Shapes the planner gives to the SM-pair kernel, against an fp32 product of the
+    dequantised operands on the GPU (the oracle's arithmetic: exact products, fp32
+    sums, per-row x per-channel scales); with a bias on the first shape."""
+    import ctypes as C
+    from microserve_b200 import _lib, kernels
+    plan = (C.c_int * 7)()
+    assert _lib.load().ms_fp8_gemm_plan(M, N, K, torch.cuda.get_device_properties(0).multi_processor_count,
+                                        plan) == 0 and plan[6] == 1, list(plan)
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    xq, sx = kernels.quantize_rows_fp8(torch.randn(M, K, generator=g, device=DEV).half())
+    wq, sw = kernels.quantize_rows_fp8((torch.randn(N, K, generator=g, device=DEV) * 0.02).half())
+    bias = torch.randn(N, generator=g, device=DEV).half() if M == 8192 else None
+    y = kernels.fp8_gemm(xq, sx, wq, sw, bias)
+    ref = (xq.float() @ wq.float().t()) * sx[:, None] * sw[None, :]
+    if bias is not None:
+        ref = ref.half().float() + bias.float()
+    tol = 2e-3 * max(1.0, ref.abs().max().item())
+    assert (y.float() - ref).abs().max().item() <= tol
+    assert (y.float() - ref).norm().item() <= 1e-3 * ref.norm().item()
+
+
 F16_GEMM_SHAPES = [
     # the LM head at 256 sequences: the full Qwen3 vocabulary, and its vocab-parallel shard at TP = 8
     (256, 151936, 4096), (256, 18992, 4096),
-    # one and a few rows (decode of small batches), split-K shards, a prefill-sized M (stream-K / whole tiles)
+    # one and a few rows (decode of small batches), split-K shards, a prefill-sized M (stream-K / whole tiles),
+    # prefill on SM pairs
     (1, 18992, 4096), (7, 1000, 64), (64, 24576, 1024), (256, 768, 4096), (300, 2048, 1024), (1024, 4096, 4096),
+    (4096, 8192, 2048),
     # 256-row x 256-token tiles with a ragged last tile; N % 8 != 0 (no bulk store); K % 64 != 0
     (200, 19000, 512), (37, 1001, 520), (129, 24576, 272),
 ]

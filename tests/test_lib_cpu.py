@@ -43,9 +43,10 @@ def test_bad_arguments_are_rejected_without_launch():
 def _plan(M, N, K, sms=148):
     import ctypes as C
     from microserve_b200 import _lib
-    out = (C.c_int * 6)()
+    out = (C.c_int * 7)()
     assert _lib.load().ms_fp8_gemm_plan(M, N, K, sms, out) == 0
-    return dict(zip(("bn", "ctas", "splits", "wide", "dp", "ch"), list(out)))
+    p = dict(zip(("bn", "ctas", "splits", "wide", "dp", "ch", "pair"), list(out)))
+    return p if p.pop("pair") == 0 else dict(p, pair=1)
 
 
 def test_gemm_schedules_of_the_8b_decode_and_prefill_shapes():
@@ -64,9 +65,12 @@ def test_gemm_schedules_of_the_8b_decode_and_prefill_shapes():
     assert _plan(256, 1536, 4096) == dict(bn=128, ctas=96, splits=4, wide=0, dp=0, ch=2)
     # one token: split-K with a 32-token tile, 3 K parts per weight tile
     assert _plan(1, 6144, 4096) == dict(bn=32, ctas=144, splits=3, wide=0, dp=0, ch=2)
-    # prefill: 256-token tiles, whole tiles when they fill the SMs evenly
-    p = _plan(8192, 4096, 4096)
-    assert p["bn"] == 256 and p["dp"] == 1 and p["ctas"] == 148
+    # prefill: 256 x 256 tiles on SM pairs, whole tiles when they fill the pairs evenly (512 tiles,
+    # 6.9 waves of 74 pairs)
+    assert _plan(8192, 4096, 4096) == dict(bn=256, ctas=148, splits=0, wide=0, dp=1, ch=2, pair=1)
+    assert _plan(8192, 24576, 4096)["pair"] == 1 and _plan(8192, 6144, 4096)["pair"] == 1
+    # too few tiles for the pairs (64 tiles), or a long K: one-SM tiles
+    assert "pair" not in _plan(1024, 4096, 4096) and "pair" not in _plan(8192, 4096, 12288)
     # K % 16 != 0: the CUDA-core kernel
     assert _plan(3, 70, 50)["bn"] == 0
 
