@@ -733,15 +733,14 @@ __device__ __forceinline__ void cluster_sync_all() {
 // 128 x 256 tile on one SM), the leader CTA (cluster rank 0) issues the MMAs,
 // which read both CTAs' halves, and each CTA's TMEM receives its 128 weight rows
 // x 256 tokens. So every output needs half the L2 -> SM bytes of the one-SM
-// tile (per-SM ingest bounds the one-SM kernel). No multicast: each CTA's TMA
+// tile (per-SM ingest bounds the one-SM kernel). Each CTA's TMA
 // loads bring only its own half, from this GPU's memory; their completion is
 // counted on the leader's barrier (.cta_group::2). Tiles are dealt whole to the
 // pairs, with double-buffered accumulators as in fp8_gemm_kernel.
 //   full[s]     leader only: both CTAs' loads of stage s landed (armed by the leader
 //               with both halves' bytes)
-//   empty[s]    each CTA: the MMAs reading stage s are done (one commit, multicast
-//               to both CTAs)
-//   acc_full[b] each CTA: accumulator b complete (multicast commit)
+//   empty[s]    each CTA: the MMAs reading stage s are done (a commit to each CTA)
+//   acc_full[b] each CTA: accumulator b complete (a commit to each CTA)
 //   acc_empty[b] leader: both CTAs' epilogues have drained accumulator b
 //               (128 local + 128 remote arrivals)
 constexpr int kPairBN = 256;                          // tokens per tile (128 per CTA)
@@ -802,13 +801,13 @@ __device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t da, uint64_t
   }
 }
 // Completion of this thread's earlier MMAs arrives on the barrier at the same
-// shared offset in both CTAs of the pair.
+// shared offset in both CTAs of the pair (one commit per CTA).
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"((unsigned short)3)
-      : "memory");
+  const uint32_t local = smem_u32(bar);
+  uint32_t peer;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 1;" : "=r"(peer) : "r"(local));
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(local) : "memory");
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer) : "memory");
 }
 
 template <int CH, bool F16>
