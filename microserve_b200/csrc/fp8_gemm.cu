@@ -743,22 +743,23 @@ __device__ __forceinline__ void cluster_sync_all() {
 //   acc_full[b] each CTA: accumulator b complete (a commit to each CTA)
 //   acc_empty[b] leader: both CTAs' epilogues have drained accumulator b
 //               (128 local + 128 remote arrivals)
-constexpr int kPairBN = 256;                          // tokens per tile (128 per CTA)
+constexpr int kPairBN = 256;                          // tokens per prefill tile (128 per CTA)
 constexpr int kPairRows = 2 * kBM;                    // weight rows per tile (128 per CTA)
 constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;        // shared address of the same object in rank 0
-template <int CH>
+template <int BN, int CH>
 struct PairCfg {
   static constexpr int kABytes = CH * kBM * kChunk;                // this CTA's weight rows
-  static constexpr int kStageBytes = kABytes + CH * (kPairBN / 2) * kChunk;
+  static constexpr int kStageBytes = kABytes + CH * (BN / 2) * kChunk;  // + this CTA's BN / 2 tokens
   static constexpr int kBarBytes = 256;
-  static constexpr int kSxBytes = 2 * kPairBN * 4;
+  static constexpr int kSxBytes = 2 * BN * 4;
+  static constexpr int kAccCols = BN <= 64 ? 64 : (BN <= 128 ? 128 : 256);  // TMEM columns per accumulator
   static constexpr int kFit = (227 * 1024 - 1024 - kBarBytes - kSxBytes) / kStageBytes;
   static constexpr int kStages = kFit > 6 ? 6 : kFit;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarBytes + kSxBytes;
-  // D=f32, A=B=e4m3 (or f16 for kind::f16), K-major, N=256, M=256
-  static constexpr uint32_t kIdesc =
-      (1u << 4) | ((uint32_t)(kPairBN >> 3) << 17) | ((uint32_t)(kPairRows >> 4) << 24);
+  // D=f32, A=B=e4m3 (or f16 for kind::f16), K-major, N=BN, M=256
+  static constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kPairRows >> 4) << 24);
   static_assert(kStages >= 2, "shared memory budget");
+  static_assert(BN % 32 == 0 && BN <= 256, "each CTA's token half: whole 8-row swizzle atoms, MMA N <= 256");
 };
 
 __device__ __forceinline__ void tma_load_pair_2d(const CUtensorMap* map, uint32_t dst, uint32_t bar, int c0, int c1) {
@@ -810,11 +811,11 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer) : "memory");
 }
 
-template <int CH, bool F16>
+template <int BN, int CH, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                          const __grid_constant__ GemmArgs args) {
-  using C = PairCfg<CH>;
+  using C = PairCfg<BN, CH>;
   extern __shared__ __align__(16) unsigned char smem_raw[];  // aligned by hand, see fp8_gemm_kernel
   const uint32_t raw_addr = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
@@ -845,7 +846,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 1) {  // the same warp in both CTAs allocates the pair's accumulators
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(512));
+                 "r"(2 * C::kAccCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -860,7 +861,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true, waited = false;
       for (int64_t t = pair; ok && t < args.T; t += pairs) {
         const int n0 = (int)(t / args.tiles_m) * kPairRows + rank * kBM;
-        const int m0 = (int)(t % args.tiles_m) * kPairBN + rank * (kPairBN / 2);
+        const int m0 = (int)(t % args.tiles_m) * BN + rank * (BN / 2);
         for (int k = 0; k < KT; ++k, ++i) {
           const int s = i % C::kStages;
           if (!mbar_wait(&empty[s], ((uint32_t)(i / C::kStages) & 1u) ^ 1u)) {
@@ -888,7 +889,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = tile & 1;
         if (!mbar_wait(&acc_empty[b], (((uint32_t)tile >> 1) & 1u) ^ 1u)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t acc = tmem + (uint32_t)(b * kPairBN);
+        const uint32_t acc = tmem + (uint32_t)(b * C::kAccCols);
         bool ok = true;
         for (int k = 0; k < KT; ++k, ++i) {
           const int s = i % C::kStages;
@@ -904,7 +905,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < kChunk / 32; ++kk) {
               const uint64_t da = da0 + (uint64_t)((c * kBM * kChunk + kk * 32) >> 4);
-              const uint64_t db = db0 + (uint64_t)((c * (kPairBN / 2) * kChunk + kk * 32) >> 4);
+              const uint64_t db = db0 + (uint64_t)((c * (BN / 2) * kChunk + kk * 32) >> 4);
               umma_pair<F16>(acc, da, db, C::kIdesc, (k > 0 || c > 0 || kk > 0) ? 1u : 0u);
             }
           }
@@ -925,20 +926,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int64_t t = pair; t < args.T; t += pairs, ++tile) {
       const int b = tile & 1;
       const int n = (int)(t / args.tiles_m) * kPairRows + rank * kBM + row;
-      const int m0 = (int)(t % args.tiles_m) * kPairBN;
-      const int cols = min(kPairBN, args.M - m0);
-      for (int j = et; j < cols; j += 128) s_sx[b * kPairBN + j] = args.sx != nullptr ? args.sx[m0 + j] : 1.f;
+      const int m0 = (int)(t % args.tiles_m) * BN;
+      const int cols = min(BN, args.M - m0);
+      for (int j = et; j < cols; j += 128) s_sx[b * BN + j] = args.sx != nullptr ? args.sx[m0 + j] : 1.f;
       const bool n_ok = n < args.N;
       const float swn = n_ok ? (args.sw != nullptr ? args.sw[n] : 1.f) : 0.f;
       const float bn = (n_ok && args.bias != nullptr) ? __half2float(args.bias[n]) : 0.f;
       if (!mbar_wait(&acc_full[b], ((uint32_t)tile >> 1) & 1u)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       epi_sync();  // s_sx filled
-      const uint32_t acc = tmem + (uint32_t)(b * kPairBN) + ((uint32_t)(q * 32) << 16);
+      const uint32_t acc = tmem + (uint32_t)(b * C::kAccCols) + ((uint32_t)(q * 32) << 16);
       for (int c0 = 0; c0 < cols; c0 += 16) {
         float v[16];
         tmem_ld16(acc + (uint32_t)c0, v);
-        out16(args, v, s_sx + b * kPairBN, swn, bn, m0, c0, cols, n, nullptr, row);
+        out16(args, v, s_sx + b * BN, swn, bn, m0, c0, cols, n, nullptr, row);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       epi_sync();  // every thread has read s_sx[b] and accumulator b
@@ -952,7 +953,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * C::kAccCols));
   }
   cluster_sync_all();  // both CTAs have released the pair's accumulators before either exits
 }
@@ -1269,13 +1270,13 @@ cudaError_t launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const CUtens
                   : launch_tc_kind<BN, CH, false>(mw, mx, my, args, stream);
 }
 
-template <int CH, bool F16>
+template <int BN, int CH, bool F16>
 cudaError_t launch_pair_kind(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& args, cudaStream_t stream) {
-  using C = PairCfg<CH>;
+  using C = PairCfg<BN, CH>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_pair_kernel<CH, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_pair_kernel<BN, CH, F16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -1295,7 +1296,16 @@ cudaError_t launch_pair_kind(const CUtensorMap& mw, const CUtensorMap& mx, const
   cfg.attrs = attr;
   cfg.numAttrs = g_pdl_enabled.load(std::memory_order_relaxed) ? 2 : 1;
   MS_COUNT_LAUNCH();
-  return cudaLaunchKernelEx(&cfg, fp8_gemm_pair_kernel<CH, F16>, mw, mx, args);
+  return cudaLaunchKernelEx(&cfg, fp8_gemm_pair_kernel<BN, CH, F16>, mw, mx, args);
+}
+
+template <int BN>
+cudaError_t launch_pair_bn(int ch, bool f16, const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& args,
+                           cudaStream_t stream) {
+  if (ch == 2)
+    return f16 ? launch_pair_kind<BN, 2, true>(mw, mx, args, stream)
+               : launch_pair_kind<BN, 2, false>(mw, mx, args, stream);
+  return f16 ? launch_pair_kind<BN, 1, true>(mw, mx, args, stream) : launch_pair_kind<BN, 1, false>(mw, mx, args, stream);
 }
 
 template <int BN>
@@ -1335,6 +1345,18 @@ struct Plan {
 Plan make_plan(int M, int N, int K, int num_sms, bool allow_pair = true) {
   Plan p{256, (K % kChunk == 0) ? 2 : 1, 1, 0, 0, 0, 0};
   const int64_t tiles_n = (N + kBM - 1) / kBM;
+  const int64_t pairs = num_sms / 2;
+  if (M > 128 && M <= 256 && tiles_n > num_sms && allow_pair && K >= 2048 && pairs >= 1) {
+    // e.g. gate/up at 256 tokens: 256 x 256 tiles on SM pairs, over all SMs (8B gate/up
+    // 30.6 us in two waves of 74 pairs vs 34.0 us for the one-SM 256 x 256 tiles on 96
+    // SMs below; B200)
+    const int64_t T2 = (N + kPairRows - 1) / kPairRows;
+    p.pair = 1;
+    p.dp = 1;
+    p.bn = 256;
+    p.ctas = (int)(2 * (T2 < pairs ? T2 : pairs));
+    return p;
+  }
   if (M > 128 && M <= 256 && tiles_n > num_sms) {  // e.g. gate/up: 256-row x 256-token tiles
     const int64_t T = (N + kWideRows - 1) / kWideRows;
     p.wide = 1;
@@ -1377,7 +1399,6 @@ Plan make_plan(int M, int N, int K, int num_sms, bool allow_pair = true) {
     // prefill: 256 x 256 tiles on SM pairs (fp8_gemm_pair_kernel) when they fill the
     // pairs evenly (B200, 8192 tokens: q/k/v 192.9 vs 223.3 us for one-SM tiles, o and
     // gate/up within 1 %, the 12288-long K of down 417 vs 395 us, so not for long K)
-    const int64_t pairs = num_sms / 2;
     const int64_t T2 = ((N + kPairRows - 1) / kPairRows) * ((M + kPairBN - 1) / kPairBN);
     const int64_t waves2 = (T2 + pairs - 1) / pairs;
     if (pairs >= 1 && T2 >= pairs && (double)T2 / ((double)waves2 * pairs) >= 0.9) {
@@ -1406,6 +1427,14 @@ Plan make_plan(int M, int N, int K, int num_sms, bool allow_pair = true) {
   if (decode && (2 * T >= num_sms || steps <= 16)) {
     p.dp = 1;
     p.ctas = (int)(T < num_sms ? T : num_sms);
+    const int64_t T2 = ((N + kPairRows - 1) / kPairRows) * ((M + 95) / 96);
+    if (M > 128 && allow_pair && K >= 2048 && T2 <= pairs) {
+      // 256 weight rows x 96 tokens on SM pairs, one wave (each SM loads 48 tokens:
+      // qkv at 256 tokens 12.7 vs 13.7 us, o 11.7 vs 12.3 us; B200)
+      p.pair = 1;
+      p.bn = 96;
+      p.ctas = (int)(2 * T2);
+    }
     return p;
   }
   const int64_t waves = (T + num_sms - 1) / num_sms;
@@ -1476,14 +1505,14 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
   const bool tma_y = rp == nullptr && N % 8 == 0 && ((uintptr_t)y & 15) == 0 && make_map(&my, y, M, N, bn, 0);
   if (!tma_y) memset(&my, 0, sizeof(my));
   if (p.pair) {
-    if (!make_map(&mw, wq, N, K, kBM, p.ch) || !make_map(&mx, xq, M, K, kPairBN / 2, p.ch))
+    if (!make_map(&mw, wq, N, K, kBM, p.ch) || !make_map(&mx, xq, M, K, p.bn / 2, p.ch))
       return cudaErrorInvalidValue;
     GemmArgs args = {};
     args.M = M;
     args.N = N;
     args.K = K;
     args.KT = (K + kChunk * p.ch - 1) / (kChunk * p.ch);
-    args.tiles_m = (M + kPairBN - 1) / kPairBN;
+    args.tiles_m = (M + p.bn - 1) / p.bn;
     args.T = (int64_t)((N + kPairRows - 1) / kPairRows) * args.tiles_m;
     args.G = p.ctas;
     args.dp = 1;
@@ -1492,9 +1521,13 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
     args.bias = (const __half*)bias;
     args.y = (__half*)y;
     args.f16 = f16 ? 1 : 0;
-    if (p.ch == 2)
-      return f16 ? launch_pair_kind<2, true>(mw, mx, args, stream) : launch_pair_kind<2, false>(mw, mx, args, stream);
-    return f16 ? launch_pair_kind<1, true>(mw, mx, args, stream) : launch_pair_kind<1, false>(mw, mx, args, stream);
+    switch (p.bn) {
+      case 64: return launch_pair_bn<64>(p.ch, f16, mw, mx, args, stream);
+      case 96: return launch_pair_bn<96>(p.ch, f16, mw, mx, args, stream);
+      case 128: return launch_pair_bn<128>(p.ch, f16, mw, mx, args, stream);
+      case 256: return launch_pair_bn<256>(p.ch, f16, mw, mx, args, stream);
+      default: return cudaErrorInvalidValue;
+    }
   }
   if (p.wide) {
     if (rp != nullptr) return cudaErrorInvalidValue;  // row-parallel outputs are never that wide

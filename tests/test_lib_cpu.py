@@ -53,11 +53,14 @@ def test_gemm_schedules_of_the_8b_decode_and_prefill_shapes():
     """The FP8 GEMM planner's choices for the bench's Qwen3-8B shapes on 148 SMs
     (the rules in csrc/fp8_gemm.cu make_plan; timings behind them in
     profiles/fp8_gemm_qwen3-8b_m256.md)."""
-    # decode, 256 tokens: qkv / o whole tiles of 96 / 64 tokens, one wave each
-    assert _plan(256, 6144, 4096) == dict(bn=96, ctas=144, splits=0, wide=0, dp=1, ch=2)
-    assert _plan(256, 4096, 4096) == dict(bn=64, ctas=128, splits=0, wide=0, dp=1, ch=2)
-    # gate_up: 96 tiles of 256 weight rows x 256 tokens
-    assert _plan(256, 24576, 4096) == dict(bn=256, ctas=96, splits=0, wide=1, dp=1, ch=1)
+    # decode, 256 tokens: qkv / o whole tiles of 256 weight rows x 96 tokens on SM pairs, one wave each
+    assert _plan(256, 6144, 4096) == dict(bn=96, ctas=144, splits=0, wide=0, dp=1, ch=2, pair=1)
+    assert _plan(256, 4096, 4096) == dict(bn=96, ctas=96, splits=0, wide=0, dp=1, ch=2, pair=1)
+    # gate_up: 96 tiles of 256 weight rows x 256 tokens on the 74 SM pairs
+    assert _plan(256, 24576, 4096) == dict(bn=256, ctas=148, splits=0, wide=0, dp=1, ch=2, pair=1)
+    # short K: whole 64-token tiles on single SMs; 256 x 256 tiles on single SMs (96 of them)
+    assert _plan(256, 4096, 1024) == dict(bn=64, ctas=128, splits=0, wide=0, dp=1, ch=2)
+    assert _plan(256, 24576, 1024) == dict(bn=256, ctas=96, splits=0, wide=1, dp=1, ch=1)
     # down (long K): split-K, 32 weight tiles x 4 K parts
     assert _plan(256, 4096, 12288) == dict(bn=256, ctas=128, splits=4, wide=0, dp=0, ch=2)
     # tensor-parallel q/k/v shards at 256 tokens: 4 K parts over 64- / 128-token tiles
