@@ -56,6 +56,12 @@ int64_t ms_launch_count(void);
  * produce or consume. Returns the previous setting. Process-wide. */
 int ms_set_pdl(int enable);
 
+/* GEMM schedules on pairs of SMs (tcgen05 cta_group::2 clusters; no reference
+ * counterpart): enabled by default; when disabled every GEMM uses one-SM tiles
+ * (the plans of ms_fp8_gemm_plan with plan[6] = 0). The engine disables them
+ * under tensor parallelism. Returns the previous setting. Process-wide. */
+int ms_set_pair_tiles(int enable);
+
 /* Reads and clears the device status word of the current device. Kernels
  * that wait on barriers give up after a bounded time, record a non-zero code
  * there (1 = tensor-core pipeline timeout, 2 = peer timeout) and return.

@@ -24,6 +24,7 @@ SIGNATURES: dict[str, tuple] = {
     "ms_last_error": (C.c_char_p, []),
     "ms_launch_count": (i64, []),
     "ms_set_pdl": (i32, [i32]),
+    "ms_set_pair_tiles": (i32, [i32]),
     "ms_argmax_workspace_size": (sz, [i64]),
     "ms_ipc_handle": (i32, [vp, vp, C.POINTER(C.c_int64)]),
     "ms_ipc_open": (i32, [vp, i64, C.POINTER(vp), C.POINTER(vp)]),

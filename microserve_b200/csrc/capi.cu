@@ -60,6 +60,8 @@ int64_t ms_launch_count(void) { return ms::g_host_launches.load(std::memory_orde
 
 int ms_set_pdl(int enable) { return ms::g_pdl_enabled.exchange(enable ? 1 : 0); }
 
+int ms_set_pair_tiles(int enable) { return ms::g_pair_tiles_enabled.exchange(enable ? 1 : 0); }
+
 int ms_get_device_status(int* status, void* stream) {
   if (status == nullptr) return fail(MS_ERR_INVALID, "ms_get_device_status: status is NULL");
   int host = 0, zero = 0;

@@ -65,6 +65,7 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 // Host: whether launches carry the programmatic-serialization attribute.
 extern std::atomic<int> g_pdl_enabled;
+extern std::atomic<int> g_pair_tiles_enabled;  // FP8/fp16 GEMM: SM-pair schedules allowed
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,

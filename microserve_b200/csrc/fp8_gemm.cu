@@ -1461,7 +1461,7 @@ void gemm_plan(int M, int N, int K, int num_sms, int* out) {
     out[4] = 1;
     return;
   }
-  const Plan p = make_plan(M, N, K, num_sms);
+  const Plan p = make_plan(M, N, K, num_sms, g_pair_tiles_enabled.load(std::memory_order_relaxed) != 0);
   out[0] = p.bn;
   out[1] = p.ctas;
   out[2] = p.splits;
@@ -1495,7 +1495,7 @@ cudaError_t launch_fp8_gemm(const void* xq, const float* sx, const void* wq, con
                          N, K, sx, sw, (const __half*)bias, (__half*)y);
   }
   // (row-parallel push and the tensor-parallel tail are written for one-SM tiles)
-  const Plan p = make_plan(M, N, K, num_sms, rp == nullptr);
+  const Plan p = make_plan(M, N, K, num_sms, rp == nullptr && g_pair_tiles_enabled.load(std::memory_order_relaxed));
   const int bn = p.bn;
   if (!p.dp && (gemm_workspace_bytes(M, N, K, num_sms) > workspace_bytes || workspace == nullptr))
     return cudaErrorInvalidValue;
