@@ -84,11 +84,11 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples taken DURING the timed region (median SM clock, throttle reasons).
+    """Clock samples taken DURING the timed region (median SM clock, throttle reasons):
+    NVML queries from a thread every 10 ms (read-only), else an nvidia-smi loop.
 
-    The sampler process is started and confirmed running (first line read)
-    before the region opens; a reader thread timestamps every line, and only
-    lines that arrive between mark_start() and mark_end() count."""
+    The sampler is running before the region opens; every sample is timestamped,
+    and only samples between mark_start() and mark_end() count."""
 
     def __init__(self, index: int, period_ms: int = 25):
         self.index, self.period_ms = index, period_ms
@@ -97,6 +97,8 @@ class ClockSampler:
 
     def __enter__(self):
         import threading
+        if self._enter_nvml():
+            return self
         q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
@@ -119,6 +121,38 @@ class ClockSampler:
         first.wait(timeout=10)
         return self
 
+    def _enter_nvml(self) -> bool:
+        """Sample through NVML in a thread (reads only): exact timestamps, a sample every
+        10 ms, so even a short timed region holds several. False if NVML is unavailable."""
+        import threading
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        except Exception:
+            return False
+        bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+        self._stop = threading.Event()
+        self._nvml = nv
+
+        def sampler():
+            while not self._stop.is_set():
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except Exception:
+                    break
+                flags = ", ".join("Active" if rs & b else "Not Active" for b in bits)
+                self._stamped.append((time.monotonic(), f"{sm}, {mx}, {pw:.1f}, {flags}"))
+                self._stop.wait(0.01)
+        self._thread = threading.Thread(target=sampler, daemon=True)
+        self._thread.start()
+        self.proc = "nvml"
+        return True
+
     def mark_start(self):
         self.t0 = time.monotonic()
 
@@ -130,12 +164,20 @@ class ClockSampler:
             return
         if self.t1 is not None:  # let the sample in flight at the end of the region arrive
             time.sleep(2 * self.period_ms / 1000)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self._thread.join(timeout=5)
+        if self.proc == "nvml":
+            self._stop.set()
+            self._thread.join(timeout=5)
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
+        else:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self._thread.join(timeout=5)
         t0 = self.t0 if self.t0 is not None else 0.0
         t1 = (self.t1 if self.t1 is not None else time.monotonic()) + 1.5 * self.period_ms / 1000
         self.lines = [l for t, l in self._stamped if t0 <= t <= t1 and l.strip()]
