@@ -78,6 +78,21 @@ def test_gemm_schedules_of_the_8b_decode_and_prefill_shapes():
     assert _plan(3, 70, 50)["bn"] == 0
 
 
+def test_pair_tile_schedules_can_be_turned_off():
+    """ms_set_pair_tiles(0) (what the engine does under tensor parallelism) gives every
+    shape a one-SM schedule; turning it back on restores the SM-pair plans."""
+    from microserve_b200 import _lib
+    lib = _lib.load()
+    prev = lib.ms_set_pair_tiles(0)
+    try:
+        for M, N, K in ((256, 6144, 4096), (256, 24576, 4096), (8192, 4096, 4096)):
+            assert "pair" not in _plan(M, N, K), (M, N, K)
+        assert _plan(256, 24576, 4096)["wide"] == 1
+    finally:
+        lib.ms_set_pair_tiles(prev)
+    assert _plan(256, 6144, 4096)["pair"] == 1
+
+
 def test_gemm_schedules_keep_cooperating_ctas_resident():
     """Split-K and stream-K CTAs wait for one another, so those schedules never
     launch more CTAs than SMs; no K part is empty."""
