@@ -210,7 +210,8 @@ def build_engine(args, cfg, max_model_len):
                             num_kvcache_blocks=args.kv_blocks,
                             tp_fused_collective=not getattr(args, "nccl_allreduce", False),
                             tp_fused_gemm=getattr(args, "tp_one_kernel", False),
-                            tp_exact_act_scale=getattr(args, "exact_act_scale", False)))
+                            tp_exact_act_scale=getattr(args, "exact_act_scale", False),
+                            gemm_pair_tiles=getattr(args, "pair_tiles", False)))
 
 
 def sync_all():
@@ -603,7 +604,7 @@ def run_ours(args):
         "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 acc, f16 activations",
         "data": "synthetic: random N(0,0.02) weights quantised to FP8, prompts U[128,1024] from random.Random(0)",
         "config": workload_config(args, batch["ctx0"]),
-        "setup": {"pdl": not args.no_pdl,
+        "setup": {"pdl": not args.no_pdl, "gemm_pair_tiles": bool(args.pair_tiles and args.gpus == 1),
                   "tp_collective": ("nccl all-reduce" if args.nccl_allreduce else
                                     "fused peer-memory all-reduce+rmsnorm+fp8") if args.gpus > 1 else None,
                   "tp_act_scale": "exact (full row)" if args.exact_act_scale else "per shard",
@@ -956,7 +957,7 @@ def run_kernel(args):
                               "unavailable": "reference not installed in baseline/_ref"}), flush=True)
             return
     else:
-        _lib.load()
+        _lib.load().ms_set_pair_tiles(1 if args.pair_tiles else 0)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     m = MODELS[args.model]
@@ -1055,6 +1056,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nccl-allreduce", action="store_true",
                     help="tensor parallel: NCCL all-reduce instead of the fused peer-memory kernel")
+    ap.add_argument("--pair-tiles", action="store_true",
+                    help="one GPU: GEMM tiles on pairs of SMs (tcgen05 cta_group::2) where the planner finds them faster")
     ap.add_argument("--tp-one-kernel", action="store_true",
                     help="tensor parallel: row-parallel GEMM pushing its rows + reduce/norm tail, one kernel")
     ap.add_argument("--exact-act-scale", action="store_true",

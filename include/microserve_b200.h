@@ -57,9 +57,10 @@ int64_t ms_launch_count(void);
 int ms_set_pdl(int enable);
 
 /* GEMM schedules on pairs of SMs (tcgen05 cta_group::2 clusters; no reference
- * counterpart): enabled by default; when disabled every GEMM uses one-SM tiles
- * (the plans of ms_fp8_gemm_plan with plan[6] = 0). The engine disables them
- * under tensor parallelism. Returns the previous setting. Process-wide. */
+ * counterpart): off by default; when enabled, 129..256-token and prefill shapes
+ * may use them (ms_fp8_gemm_plan reports plan[6] = 1), otherwise every GEMM uses
+ * one-SM tiles. The engine enables them on one GPU when Config.gemm_pair_tiles
+ * is set. Returns the previous setting. Process-wide. */
 int ms_set_pair_tiles(int enable);
 
 /* Reads and clears the device status word of the current device. Kernels

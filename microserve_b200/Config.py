@@ -15,6 +15,9 @@
                          input row (o_proj, down_proj) by its amax over the
                          full row, as a single GPU does (one all-reduce max of
                          a float per row), instead of the local shard's amax;
+  gemm_pair_tiles      - on one GPU, let the FP8 / fp16 GEMMs use tiles on
+                         pairs of SMs (tcgen05 cta_group::2) where they are
+                         faster (129..256 tokens, prefill);
   load_format          - "safetensors" (model_dir holds the checkpoint) or
                          "dummy" (seeded N(0, 0.02) random weights of the
                          shape in model_dir/config.json or `hf_config`);
@@ -51,6 +54,7 @@ class Config:
     tp_fused_collective: bool = True
     tp_fused_gemm: bool = False
     tp_exact_act_scale: bool = False
+    gemm_pair_tiles: bool = False
     load_format: str = "safetensors"
     hf_config: object = None
 

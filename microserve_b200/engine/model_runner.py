@@ -86,10 +86,10 @@ class ModelRunner:
                                f"{tp.tp_size()} ranks (call utils.dist.init_tensor_parallel first)")
 
         tp.set_exact_act_scale(config.tp_exact_act_scale)
-        # GEMMs on SM pairs (thread-block clusters) are used on one GPU only; under tensor
+        # GEMMs on SM pairs (thread-block clusters): opt-in, one GPU only; under tensor
         # parallelism every GEMM keeps one-SM tiles, the schedules verified with the
         # peer-memory collectives around them
-        _lib.load().ms_set_pair_tiles(1 if tp.tp_size() == 1 else 0)
+        _lib.load().ms_set_pair_tiles(1 if (tp.tp_size() == 1 and config.gemm_pair_tiles) else 0)
         self.hf_config = hf = _load_hf_config(config)
         self.num_kv_heads = hf.num_key_value_heads // tp.tp_size()
         self.head_dim = getattr(hf, "head_dim", None) or hf.hidden_size // hf.num_attention_heads

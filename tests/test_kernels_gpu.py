@@ -138,6 +138,8 @@ PAIR_GEMM_SHAPES = [
     # prefill-sized tiles on SM pairs (tcgen05 cta_group::2, 256 x 256 per pair): 2-chunk stages; ragged M,
     # N and K % 128 != 0 (1-chunk stages); 96 weight tiles; one K step per tile
     (8192, 4096, 4096), (8000, 4000, 1040), (2048, 24576, 1024), (4096, 9472, 256),
+    # 129..256 tokens: 256 weight rows x 96 tokens (qkv / o; a ragged token tile), 256 x 256 over all pairs
+    (256, 6144, 4096), (200, 4096, 2048), (256, 24576, 4096),
 ]
 
 
@@ -148,14 +150,20 @@ def test_fp8_gemm_on_sm_pairs(M, N, K):
     sums, per-row x per-channel scales); with a bias on the first shape."""
     import ctypes as C
     from microserve_b200 import _lib, kernels
-    plan = (C.c_int * 7)()
-    assert _lib.load().ms_fp8_gemm_plan(M, N, K, torch.cuda.get_device_properties(0).multi_processor_count,
-                                        plan) == 0 and plan[6] == 1, list(plan)
-    g = torch.Generator(device=DEV).manual_seed(M + N + K)
-    xq, sx = kernels.quantize_rows_fp8(torch.randn(M, K, generator=g, device=DEV).half())
-    wq, sw = kernels.quantize_rows_fp8((torch.randn(N, K, generator=g, device=DEV) * 0.02).half())
-    bias = torch.randn(N, generator=g, device=DEV).half() if M == 8192 else None
-    y = kernels.fp8_gemm(xq, sx, wq, sw, bias)
+    lib = _lib.load()
+    prev = lib.ms_set_pair_tiles(1)
+    try:
+        plan = (C.c_int * 7)()
+        assert lib.ms_fp8_gemm_plan(M, N, K, torch.cuda.get_device_properties(0).multi_processor_count,
+                                    plan) == 0 and plan[6] == 1, list(plan)
+        g = torch.Generator(device=DEV).manual_seed(M + N + K)
+        xq, sx = kernels.quantize_rows_fp8(torch.randn(M, K, generator=g, device=DEV).half())
+        wq, sw = kernels.quantize_rows_fp8((torch.randn(N, K, generator=g, device=DEV) * 0.02).half())
+        bias = torch.randn(N, generator=g, device=DEV).half() if M == 8192 else None
+        y = kernels.fp8_gemm(xq, sx, wq, sw, bias)
+        torch.cuda.synchronize()
+    finally:
+        lib.ms_set_pair_tiles(prev)
     ref = (xq.float() @ wq.float().t()) * sx[:, None] * sw[None, :]
     if bias is not None:
         ref = ref.half().float() + bias.float()
@@ -174,6 +182,26 @@ F16_GEMM_SHAPES = [
     # 256-row x 256-token tiles with a ragged last tile; N % 8 != 0 (no bulk store); K % 64 != 0
     (200, 19000, 512), (37, 1001, 520), (129, 24576, 272),
 ]
+
+
+def test_f16_gemm_on_sm_pairs():
+    """The LM head's fp16 GEMM with the SM-pair schedule on (256 x 256 tiles over all
+    pairs; kind::f16 with cta_group::2) against an fp32 product."""
+    from microserve_b200 import _lib, kernels
+    lib = _lib.load()
+    g = torch.Generator(device=DEV).manual_seed(11)
+    for M, N, K in ((256, 151936, 4096), (4096, 8192, 2048)):
+        x = torch.randn(M, K, generator=g, device=DEV).half()
+        w = (torch.randn(N, K, generator=g, device=DEV) * 0.02).half()
+        prev = lib.ms_set_pair_tiles(1)
+        try:
+            y = kernels.f16_gemm(x, w)
+            torch.cuda.synchronize()
+        finally:
+            lib.ms_set_pair_tiles(prev)
+        ref = x.float() @ w.float().t()
+        tol = 2e-3 * max(1.0, ref.abs().max().item())
+        assert (y.float() - ref).abs().max().item() <= tol, (M, N, K)
 
 
 @pytest.mark.parametrize("M,N,K", F16_GEMM_SHAPES)

@@ -52,15 +52,15 @@ def _plan(M, N, K, sms=148):
 def test_gemm_schedules_of_the_8b_decode_and_prefill_shapes():
     """The FP8 GEMM planner's choices for the bench's Qwen3-8B shapes on 148 SMs
     (the rules in csrc/fp8_gemm.cu make_plan; timings behind them in
-    profiles/fp8_gemm_qwen3-8b_m256.md)."""
-    # decode, 256 tokens: qkv / o whole tiles of 256 weight rows x 96 tokens on SM pairs, one wave each
-    assert _plan(256, 6144, 4096) == dict(bn=96, ctas=144, splits=0, wide=0, dp=1, ch=2, pair=1)
-    assert _plan(256, 4096, 4096) == dict(bn=96, ctas=96, splits=0, wide=0, dp=1, ch=2, pair=1)
-    # gate_up: 96 tiles of 256 weight rows x 256 tokens on the 74 SM pairs
-    assert _plan(256, 24576, 4096) == dict(bn=256, ctas=148, splits=0, wide=0, dp=1, ch=2, pair=1)
-    # short K: whole 64-token tiles on single SMs; 256 x 256 tiles on single SMs (96 of them)
-    assert _plan(256, 4096, 1024) == dict(bn=64, ctas=128, splits=0, wide=0, dp=1, ch=2)
-    assert _plan(256, 24576, 1024) == dict(bn=256, ctas=96, splits=0, wide=1, dp=1, ch=1)
+    profiles/fp8_gemm_qwen3-8b_m256.md), with one-SM tiles (the default) and with the
+    SM-pair schedules turned on (ms_set_pair_tiles)."""
+    from microserve_b200 import _lib
+    lib = _lib.load()
+    # decode, 256 tokens: qkv / o whole tiles of 96 / 64 tokens, one wave each
+    assert _plan(256, 6144, 4096) == dict(bn=96, ctas=144, splits=0, wide=0, dp=1, ch=2)
+    assert _plan(256, 4096, 4096) == dict(bn=64, ctas=128, splits=0, wide=0, dp=1, ch=2)
+    # gate_up: 96 tiles of 256 weight rows x 256 tokens
+    assert _plan(256, 24576, 4096) == dict(bn=256, ctas=96, splits=0, wide=1, dp=1, ch=1)
     # down (long K): split-K, 32 weight tiles x 4 K parts
     assert _plan(256, 4096, 12288) == dict(bn=256, ctas=128, splits=4, wide=0, dp=0, ch=2)
     # tensor-parallel q/k/v shards at 256 tokens: 4 K parts over 64- / 128-token tiles
@@ -68,29 +68,46 @@ def test_gemm_schedules_of_the_8b_decode_and_prefill_shapes():
     assert _plan(256, 1536, 4096) == dict(bn=128, ctas=96, splits=4, wide=0, dp=0, ch=2)
     # one token: split-K with a 32-token tile, 3 K parts per weight tile
     assert _plan(1, 6144, 4096) == dict(bn=32, ctas=144, splits=3, wide=0, dp=0, ch=2)
-    # prefill: 256 x 256 tiles on SM pairs, whole tiles when they fill the pairs evenly (512 tiles,
-    # 6.9 waves of 74 pairs)
-    assert _plan(8192, 4096, 4096) == dict(bn=256, ctas=148, splits=0, wide=0, dp=1, ch=2, pair=1)
-    assert _plan(8192, 24576, 4096)["pair"] == 1 and _plan(8192, 6144, 4096)["pair"] == 1
-    # too few tiles for the pairs (64 tiles), or a long K: one-SM tiles
-    assert "pair" not in _plan(1024, 4096, 4096) and "pair" not in _plan(8192, 4096, 12288)
+    # prefill: 256-token tiles, whole tiles when they fill the SMs evenly
+    p = _plan(8192, 4096, 4096)
+    assert p["bn"] == 256 and p["dp"] == 1 and p["ctas"] == 148
     # K % 16 != 0: the CUDA-core kernel
     assert _plan(3, 70, 50)["bn"] == 0
 
-
-def test_pair_tile_schedules_can_be_turned_off():
-    """ms_set_pair_tiles(0) (what the engine does under tensor parallelism) gives every
-    shape a one-SM schedule; turning it back on restores the SM-pair plans."""
-    from microserve_b200 import _lib
-    lib = _lib.load()
-    prev = lib.ms_set_pair_tiles(0)
+    prev = lib.ms_set_pair_tiles(1)
     try:
-        for M, N, K in ((256, 6144, 4096), (256, 24576, 4096), (8192, 4096, 4096)):
-            assert "pair" not in _plan(M, N, K), (M, N, K)
-        assert _plan(256, 24576, 4096)["wide"] == 1
+        # decode, 256 tokens: qkv / o as 256 weight rows x 96 tokens on SM pairs, one wave each
+        assert _plan(256, 6144, 4096) == dict(bn=96, ctas=144, splits=0, wide=0, dp=1, ch=2, pair=1)
+        assert _plan(256, 4096, 4096) == dict(bn=96, ctas=96, splits=0, wide=0, dp=1, ch=2, pair=1)
+        # gate_up: 96 tiles of 256 weight rows x 256 tokens on the 74 SM pairs
+        assert _plan(256, 24576, 4096) == dict(bn=256, ctas=148, splits=0, wide=0, dp=1, ch=2, pair=1)
+        # short K: one-SM tiles as before; down keeps split-K
+        assert _plan(256, 4096, 1024) == dict(bn=64, ctas=128, splits=0, wide=0, dp=1, ch=2)
+        assert _plan(256, 24576, 1024) == dict(bn=256, ctas=96, splits=0, wide=1, dp=1, ch=1)
+        assert _plan(256, 4096, 12288) == dict(bn=256, ctas=128, splits=4, wide=0, dp=0, ch=2)
+        # prefill: 256 x 256 tiles on SM pairs when they fill the pairs evenly (512 tiles, 6.9 waves)
+        assert _plan(8192, 4096, 4096) == dict(bn=256, ctas=148, splits=0, wide=0, dp=1, ch=2, pair=1)
+        assert _plan(8192, 24576, 4096)["pair"] == 1 and _plan(8192, 6144, 4096)["pair"] == 1
+        # too few tiles for the pairs (64 tiles), or a long K: one-SM tiles
+        assert "pair" not in _plan(1024, 4096, 4096) and "pair" not in _plan(8192, 4096, 12288)
     finally:
         lib.ms_set_pair_tiles(prev)
-    assert _plan(256, 6144, 4096)["pair"] == 1
+
+
+def test_pair_tile_schedules_are_opt_in():
+    """Off by default: every shape has a one-SM schedule until ms_set_pair_tiles(1);
+    turning it off again restores them."""
+    from microserve_b200 import _lib
+    lib = _lib.load()
+    for M, N, K in ((256, 6144, 4096), (256, 24576, 4096), (8192, 4096, 4096)):
+        assert "pair" not in _plan(M, N, K), (M, N, K)
+    prev = lib.ms_set_pair_tiles(1)
+    assert prev == 0
+    try:
+        assert _plan(256, 6144, 4096)["pair"] == 1
+    finally:
+        lib.ms_set_pair_tiles(0)
+    assert "pair" not in _plan(256, 6144, 4096)
 
 
 def test_gemm_schedules_keep_cooperating_ctas_resident():
