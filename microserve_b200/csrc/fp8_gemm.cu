@@ -26,6 +26,12 @@
 // CTA prologue may overlap the preceding grid; everything that reads its
 // results (activations, token scales, workspace, output) waits for it.
 //
+// Two more tile shapes: 256 weight rows x 256 tokens on one SM (fp8_gemm_wide_kernel,
+// two M = 128 MMAs sharing each token stage) and, opt-in (ms_set_pair_tiles), 256
+// weight rows x BN tokens on a pair of SMs (fp8_gemm_pair_kernel, tcgen05 cta_group::2).
+// Every kernel also takes fp16 operands (kind::f16, K counted in bytes, no scales) for
+// the LM head (ms_f16_gemm).
+//
 // Every wait is bounded (common.cuh: mbar_wait); on a timeout the kernel
 // records a device status, skips the rest and still frees its TMEM.
 #include <mutex>
