@@ -40,6 +40,19 @@ def test_bad_arguments_are_rejected_without_launch():
     assert lib.ms_store_kv_fp8(None, None, 1, 8, 64, None, None, None, None, None, None) == _lib.MS_ERR_UNSUPPORTED
 
 
+def test_f16_gemm_arguments_are_checked_without_launch():
+    """ms_f16_gemm (the LM head's GEMM) rejects bad sizes, null pointers and K % 8 != 0
+    before touching the GPU; its workspace query is host-only."""
+    from microserve_b200 import _lib
+    lib = _lib.load()
+    assert lib.ms_f16_gemm(None, None, None, 4, 4, 0, None, 0, None) == _lib.MS_ERR_INVALID
+    assert lib.ms_f16_gemm(None, None, None, 4, 4, 8, None, 0, None) == _lib.MS_ERR_INVALID
+    assert b"null" in lib.ms_last_error()
+    assert lib.ms_f16_gemm(8, 8, 8, 4, 4, 12, None, 0, None) == _lib.MS_ERR_UNSUPPORTED
+    assert lib.ms_f16_gemm(None, None, None, 0, 4, 8, None, 0, None) == 0  # nothing to do
+    assert lib.ms_f16_gemm_workspace_size(256, 4096, 4096) >= 0
+
+
 def _plan(M, N, K, sms=148):
     import ctypes as C
     from microserve_b200 import _lib
