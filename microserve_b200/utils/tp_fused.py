@@ -102,18 +102,20 @@ class TpFused:
         """Row-parallel FP8 GEMM + all-reduce + residual add + RMSNorm + FP8 quantisation:
         returns (xq [rows, H] e4m3, sx [rows] fp32) of the normalised rows, or with
         want_fp16 the fp16 rows [rows, H]. With fused_gemm one kernel
-        (ms_fp8_gemm_rowpar_ar_rmsnorm); otherwise the GEMM writes this rank's partial
-        output locally and ms_tp_allreduce_rmsnorm_fp8 does the rest."""
+        (ms_fp8_gemm_rowpar_ar_rmsnorm); otherwise the GEMM pushes each output row to the
+        rank that owns it (ms_fp8_gemm_rowpar) and ms_tp_allreduce_rmsnorm_fp8 does the
+        rest on the pushed rows (B200, 256 rows: 26.6 vs 27.7 us at TP=2 and 24.4 vs
+        26.0 us at TP=8 for a local partial + the op pushing it; the same bits)."""
         from microserve_b200 import kernels
         M, K = xq.shape
         if wq.shape != (self.H, K):
             raise ValueError(f"rowpar_gemm_norm: weight must be [{self.H}, {K}]")
         self._check(M, residual)
         if not self.fused_gemm:
-            kernels.fp8_gemm(xq, sx, wq, sw, out=self.partial(M))
+            self.rowpar_gemm(xq, sx, wq, sw)
             if want_fp16:
-                return self.allreduce_norm_fp16(M, residual, weight, eps)
-            return self.allreduce_norm_fp8(M, residual, weight, eps)
+                return self.allreduce_norm_fp16(M, residual, weight, eps, pushed=True)
+            return self.allreduce_norm_fp8(M, residual, weight, eps, pushed=True)
         kernels.fp8_gemm_rowpar_ar_rmsnorm(xq, sx, wq, sw, self.bases, self.rank, self.world, self.R, residual,
                                            weight, eps, want_fp16)
         if want_fp16:
