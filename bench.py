@@ -609,7 +609,7 @@ def run_ours(args):
                                     "fused peer-memory all-reduce+rmsnorm+fp8") if args.gpus > 1 else None,
                   "tp_act_scale": "exact (full row)" if args.exact_act_scale else "per shard",
                   "tp_row_parallel": ("one kernel: GEMM pushing rows + reduce/norm tail" if args.tp_one_kernel else
-                                      "GEMM + separate reduce/norm op") if args.gpus > 1 else None},
+                                      "GEMM pushing rows + separate reduce/norm op") if args.gpus > 1 else None},
         "roofline": dict(roof, peak_kind=f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s"),
         "kernels": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in v.items()
